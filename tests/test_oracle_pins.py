@@ -1,0 +1,124 @@
+"""Pins the CPU oracle against the reference's known answers.
+
+The scenarios (tests/golden/scenarios.py) are the reference's own integration
+test answers (src/tests/integration/test_vec_market.py) plus ring-wrap and
+overflow cases derived by hand from src/order_matching/market.cu.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from golden.scenarios import SCENARIOS, FILL_FIELDS
+
+_ORC_FILL = dict(price="fill_prices", size="fill_sizes", customer_id="fill_customer_ids",
+                 quoter_id="fill_quoter_ids", is_sell_quote="fill_is_sell_quote",
+                 quote_size="fill_quote_sizes", tid="fill_tid", quote_tid="fill_quote_tid")
+
+
+def run_oracle_scenario(sc):
+    N, L, O, F, C = sc["dims"]
+    mkt = oracle.OracleMarket(N, L, O, F, C)
+    fills = mkt.new_fill_batch()
+    bbos = mkt.new_bbo_batch()
+    for step in sc["steps"]:
+        q = [np.array(x, np.int32) for x in step["q"]]
+        mkt.add_two_sided_quotes(*q, fills)
+        exp = step.get("expect")
+        if not exp:
+            continue
+        if "fill_counts" in exp:
+            assert fills["fill_counts"].tolist() == exp["fill_counts"]
+        for (m, k), want in exp.get("fills", {}).items():
+            for f, v in want.items():
+                assert f in FILL_FIELDS
+                got = fills[_ORC_FILL[f]][m, k]
+                assert (bool(got) if f == "is_sell_quote" else int(got)) == v, (sc["name"], m, k, f)
+        if "bbo" in exp:
+            mkt.get_bbos(bbos)
+            got = list(zip(bbos["best_bid_prices"].tolist(), bbos["best_bid_sizes"].tolist(),
+                           bbos["best_ask_prices"].tolist(), bbos["best_ask_sizes"].tolist()))
+            assert got == [tuple(t) for t in exp["bbo"]], sc["name"]
+        for (m, c), (pos, cash) in exp.get("portfolios", {}).items():
+            assert mkt.customer_portfolios[m, c].tolist() == [pos, cash]
+    return mkt
+
+
+@pytest.mark.parametrize("sc", SCENARIOS, ids=[s["name"] for s in SCENARIOS])
+def test_oracle_known_answers(sc):
+    run_oracle_scenario(sc)
+
+
+def test_oracle_to_string():
+    # test_vec_market.py:416-439
+    mkt = oracle.OracleMarket(2, 128, 1024, 512)
+    fills = mkt.new_fill_batch()
+    mkt.add_two_sided_quotes(np.array([50, 60], np.int32), np.array([100, 200], np.int32),
+                             np.array([55, 65], np.int32), np.array([150, 250], np.int32),
+                             np.array([0, 1], np.int32), fills)
+    s = mkt.to_string(0)
+    for sub in ("sell orders", "buy orders", "px 50", "px 55", "sz 100", "sz 150"):
+        assert sub in s
+    assert mkt.to_string(5).startswith("Error: Invalid market_id 5")
+
+
+def test_oracle_reset_and_clear():
+    mkt = oracle.OracleMarket(3, 32, 8, 8, 4)
+    fills = mkt.new_fill_batch()
+    q = [np.array(v, np.int32) for v in ([5, 6, 7], [1, 2, 3], [9, 9, 9], [4, 4, 4], [0, 1, 2])]
+    mkt.add_two_sided_quotes(*q, fills)
+    q2 = [np.array(v, np.int32) for v in ([9, 9, 9], [2, 2, 2], [0, 0, 0], [0, 0, 0], [3, 3, 3])]
+    mkt.add_two_sided_quotes(*q2, fills)
+    assert fills["fill_counts"].tolist() == [1, 1, 1]
+    port = mkt.customer_portfolios.copy()
+    mkt.clear_quotes(np.array([True, False, True]))
+    st = mkt.state()
+    assert (st["bid_heads"][[0, 2]] == -1).all() and (st["order_next"][[0, 2]] == -1).all()
+    assert st["order_next_slots"].tolist() == [0, 3, 0]
+    assert (st["customer_portfolios"] == port).all()  # kept by ClearQuotes
+    assert mkt.global_tid_counter == 4
+    mkt.reset()
+    st = mkt.state()
+    assert (st["ask_heads"] == -1).all() and (st["customer_portfolios"] == 0).all()
+    assert mkt.global_tid_counter == 0
+    # order records survive Reset (market.cu:704-706)
+    assert st["order_sizes"][:, :3].tolist() == [[1, 2, 0], [2, 2, 0], [3, 2, 0]]
+
+
+def test_oracle_last_prices():
+    mkt = oracle.OracleMarket(2, 64, 16, 16, 4)
+    fills, bbos = mkt.new_fill_batch(), mkt.new_bbo_batch()
+    q = [np.array(v, np.int32) for v in ([30, 30], [5, 5], [40, 40], [5, 5], [0, 0])]
+    mkt.add_two_sided_quotes(*q, fills)
+    q = [np.array(v, np.int32) for v in ([0, 41], [0, 9], [29, 0], [3, 0], [1, 1])]
+    mkt.add_two_sided_quotes(*q, fills)
+    mkt.update_last_prices(bbos, fills)
+    # market 0: ask 29 hits the resting bid 30 -> price 30; market 1: bid 41
+    # lifts the resting ask 40 -> price 40
+    assert bbos["last_prices"].tolist() == [30, 40]
+    q = [np.array(v, np.int32) for v in ([0, 0], [0, 0], [0, 0], [0, 0], [1, 1])]
+    mkt.add_two_sided_quotes(*q, fills)
+    mkt.update_last_prices(bbos, fills)   # no fills: carried over (market.cu:785)
+    assert bbos["last_prices"].tolist() == [30, 40]
+
+
+def test_quote_stream_ranges_and_shard_invariance():
+    from astra_cuda import workloads
+    for cfg in (0, 2, 3, 4):
+        p = workloads.CONFIGS[cfg]["gen"]
+        full = oracle.OracleQuoteGen(p, 0, 256)
+        lo = oracle.OracleQuoteGen(p, 0, 100)
+        hi = oracle.OracleQuoteGen(p, 100, 156)
+        for t in range(30):
+            a = full.step()
+            b, c = lo.step(), hi.step()
+            for x, y, z in zip(a, b, c):
+                assert (x == np.concatenate([y, z])).all()
+            bp, bs, ap, as_, cid = a
+            assert (cid == t % p["cid_cycle"]).all()
+            assert ((bs == 0) | ((bs >= 1) & (bs <= (100 if p["kind"] == 0 else 1000)))).all()
+            assert (bp >= 0).all() and (ap < 128).all()
+        if p["kind"] == 0:
+            assert (full.mid >= p["mid_lo"]).all() and (full.mid <= p["mid_hi"]).all()
+        # roughly 10 % of sides absent
+        frac = float((bs == 0).mean())
+        assert 0.02 < frac < 0.25

@@ -1,0 +1,94 @@
+"""Builds the CUDA library ``_lib/libastra_market.so`` for sm_100a.
+
+``python -m astra_cuda._build`` (or ``__graft_entry__.build()``) compiles
+``csrc/am_engine.cu`` with nvcc into the package, in-tree, with the CUDA
+runtime linked statically.  A digest of the sources is stored beside the
+library so an up-to-date build is not repeated.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT_DIR = os.path.dirname(PKG_DIR)                 # astra-cuda_b200/
+REPO_DIR = os.path.dirname(ROOT_DIR)
+CSRC_DIR = os.path.join(ROOT_DIR, "csrc")
+INCLUDE_DIR = os.path.join(REPO_DIR, "include")
+LIB_DIR = os.path.join(PKG_DIR, "_lib")
+LIB_PATH = os.path.join(LIB_DIR, "libastra_market.so")
+DIGEST_PATH = LIB_PATH + ".digest"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
+              "-cudart", "static", "-Xptxas", "-warn-spills"]
+
+
+def _sources():
+    srcs = sorted(os.path.join(CSRC_DIR, f) for f in os.listdir(CSRC_DIR)
+                  if f.endswith((".cu", ".cuh", ".h")))
+    srcs.append(os.path.join(INCLUDE_DIR, "astra_market.h"))
+    return srcs
+
+
+def source_digest() -> str:
+    h = hashlib.sha256()
+    for p in _sources():
+        h.update(os.path.basename(p).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(ARCH_FLAGS + NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
+def is_current() -> bool:
+    if not os.path.exists(LIB_PATH) or not os.path.exists(DIGEST_PATH):
+        return False
+    with open(DIGEST_PATH) as f:
+        return f.read().strip() == source_digest()
+
+
+def nvcc() -> str | None:
+    cand = shutil.which("nvcc")
+    if cand:
+        return cand
+    p = "/usr/local/cuda/bin/nvcc"
+    return p if os.path.exists(p) else None
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile the library if the sources changed; return its path."""
+    if not force and is_current():
+        return LIB_PATH
+    exe = nvcc()
+    if exe is None:
+        raise RuntimeError("nvcc not found: cannot build the astra_cuda CUDA library")
+    os.makedirs(LIB_DIR, exist_ok=True)
+    import fcntl
+    with open(os.path.join(LIB_DIR, ".build.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)  # one builder when several ranks start together
+        if not force and is_current():
+            return LIB_PATH
+        return _compile(exe, verbose)
+
+
+def _compile(exe: str, verbose: bool) -> str:
+    tmp = LIB_PATH + f".tmp{os.getpid()}"
+    cmd = [exe, *NVCC_FLAGS, *ARCH_FLAGS, "-I", INCLUDE_DIR, "-I", CSRC_DIR,
+           "-o", tmp, os.path.join(CSRC_DIR, "am_engine.cu")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed building libastra_market.so:\n" + res.stderr[-4000:])
+    os.replace(tmp, LIB_PATH)
+    with open(DIGEST_PATH, "w") as f:
+        f.write(source_digest())
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

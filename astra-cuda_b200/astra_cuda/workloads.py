@@ -59,3 +59,37 @@ def algorithmic_bytes(n_markets, L, n_ins, n_fill, n_rm, n_empty, with_bbo,
     if with_pos64:
         b += 16 * n_touch
     return b
+
+
+class DeviceQuoteStream:
+    """Quotes of one configuration for markets with global ids
+    [market0, market0+n), drawn on the GPU by the library's ``quotegen``
+    kernel.  ``take(k)`` returns the next k steps as int32 ``[k, 5, n]``
+    (bid_px, bid_sz, ask_px, ask_sz, customer_ids); ``q[s, j]`` is contiguous,
+    so it can be passed straight to ``add_two_sided_quotes``."""
+
+    def __init__(self, gen: dict, market0: int, n: int, device):
+        import torch
+        from . import _native
+        self._native = _native
+        self.gen = _native.QuoteGen(int(gen["seed"]), int(gen["kind"]), int(gen["walk"]),
+                                    int(gen["mid_lo"]), int(gen["mid_hi"]),
+                                    int(gen["cid_cycle"]), 0)
+        self.market0, self.n = int(market0), int(n)
+        self.device = torch.device(device)
+        self.mid = torch.zeros((self.n,), dtype=torch.int32, device=self.device)
+        self.step = 0
+
+    def take(self, k: int, out=None):
+        import ctypes
+        import torch
+        if out is None:
+            out = torch.empty((k, 5, self.n), dtype=torch.int32, device=self.device)
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        rc = self._native.lib().am_generate_quotes(
+            idx, ctypes.byref(self.gen), self.step, k, self.market0, self.n,
+            self.mid.data_ptr() or None, out.data_ptr() or None,
+            torch.cuda.current_stream(self.device).cuda_stream)
+        self._native.check(rc, "generate_quotes")
+        self.step += k
+        return out

@@ -1,0 +1,382 @@
+// C ABI of the matching engine (include/astra_market.h): argument checks,
+// device guard, launches, error reporting.  No allocation happens here; all
+// buffers are the caller's.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "am_kernels.cuh"
+#include "astra_market.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return AM_OK;
+}
+
+// Sets `device` current for the call and restores the caller's device after
+// (the reference leaves the device changed, market.cu:464).
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != device) err = cudaSetDevice(device);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(AM_ERR_CUDA, "CUDA error in %s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+int check_dims(const am_dims* d) {
+  if (!d) return fail(AM_ERR_INVALID, "dims is NULL");
+  // VecMarket::VecMarket checks, market.cu:338-342
+  if (d->num_markets > AM_MAX_MARKETS)
+    return fail(AM_ERR_INVALID, "num_markets <= MAX_MARKETS (num_markets = %d, MAX_MARKETS = %d)",
+                d->num_markets, AM_MAX_MARKETS);
+  if (d->max_price_levels > AM_PRICE_LEVELS)
+    return fail(AM_ERR_INVALID,
+                "max_price_levels <= PRICE_LEVELS (max_price_levels = %d, PRICE_LEVELS = %d)",
+                d->max_price_levels, AM_PRICE_LEVELS);
+  if (d->max_active_orders_per_market > AM_MAX_ACTIVE_ORDERS_PER_MARKET)
+    return fail(AM_ERR_INVALID,
+                "max_active_orders_per_market <= MAX_ACTIVE_ORDERS_PER_MARKET "
+                "(max_active_orders_per_market = %d, MAX_ACTIVE_ORDERS_PER_MARKET = %d)",
+                d->max_active_orders_per_market, AM_MAX_ACTIVE_ORDERS_PER_MARKET);
+  if (d->max_active_fills_per_market > AM_MAX_ACTIVE_FILLS_PER_MARKET)
+    return fail(AM_ERR_INVALID,
+                "max_active_fills_per_market <= MAX_ACTIVE_FILLS_PER_MARKET "
+                "(max_active_fills_per_market = %d, MAX_ACTIVE_FILLS_PER_MARKET = %d)",
+                d->max_active_fills_per_market, AM_MAX_ACTIVE_FILLS_PER_MARKET);
+  if (d->num_customers > AM_MAX_CUSTOMERS)
+    return fail(AM_ERR_INVALID, "num_customers <= MAX_CUSTOMERS (num_customers = %d, MAX_CUSTOMERS = %d)",
+                d->num_customers, AM_MAX_CUSTOMERS);
+  // negative sizes fail in the reference's tensor allocation; O = 0 would be a
+  // division by zero in add_orders_kernel (market.cu:46)
+  if (d->num_markets < 0 || d->max_price_levels < 0 || d->max_active_fills_per_market < 0 ||
+      d->num_customers < 0)
+    return fail(AM_ERR_INVALID, "sizes must be non-negative (N=%d L=%d F=%d C=%d)",
+                d->num_markets, d->max_price_levels, d->max_active_fills_per_market,
+                d->num_customers);
+  if (d->max_active_orders_per_market < 1)
+    return fail(AM_ERR_INVALID, "max_active_orders_per_market >= 1 (max_active_orders_per_market = %d)",
+                d->max_active_orders_per_market);
+  return AM_OK;
+}
+
+int check_market(const am_market* mk) {
+  if (!mk) return fail(AM_ERR_INVALID, "market is NULL");
+  int rc = check_dims(&mk->dims);
+  if (rc) return rc;
+  if (!mk->book) return fail(AM_ERR_INVALID, "book is NULL");
+  if (reinterpret_cast<uintptr_t>(mk->book) % 256)
+    return fail(AM_ERR_INVALID, "book must be 256-byte aligned");
+  if (mk->dims.num_customers > 0 && mk->dims.num_markets > 0 && !mk->portfolios)
+    return fail(AM_ERR_INVALID, "portfolios is NULL");
+  if (mk->device < 0) return fail(AM_ERR_INVALID, "device_id >= 0 (device_id = %d)", mk->device);
+  return AM_OK;
+}
+
+inline am::BookView view(const am_market* mk) {
+  return am::view_of(mk->book, mk->dims.num_markets, mk->dims.max_price_levels,
+                     mk->dims.max_active_orders_per_market);
+}
+
+inline unsigned blocks_for(int64_t n) {
+  return (unsigned)((n + am::kBlock - 1) / am::kBlock);
+}
+
+inline unsigned grid_stride_blocks(int64_t n) {
+  int64_t b = (n + am::kBlock - 1) / am::kBlock;
+  const int64_t cap = 148 * 16;  // 16 resident blocks of 256 on each of 148 SMs
+  return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int check_range(const am_dims& d, int32_t market0, int32_t count) {
+  if (market0 < 0 || count < 0 || (int64_t)market0 + count > d.num_markets)
+    return fail(AM_ERR_INVALID, "market range [%d, %d) outside [0, %d)", market0,
+                market0 + count, d.num_markets);
+  return AM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* am_last_error(void) { return g_last_error.c_str(); }
+
+int32_t am_abi_version(void) { return AM_ABI_VERSION; }
+
+int am_validate_dims(const am_dims* dims) {
+  int rc = check_dims(dims);
+  return rc ? rc : ok();
+}
+
+int am_book_bytes(const am_dims* dims, uint64_t* bytes) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  if (!bytes) return fail(AM_ERR_INVALID, "bytes is NULL");
+  *bytes = am::layout_of(dims->num_markets, dims->max_price_levels,
+                         dims->max_active_orders_per_market).total;
+  return ok();
+}
+
+int am_book_init(const am_market* mk, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  const am_dims& d = mk->dims;
+  const am::Layout l = am::layout_of(d.num_markets, d.max_price_levels, d.max_active_orders_per_market);
+  char* b = static_cast<char*>(mk->book);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(b, 0, l.off_levels, s);  // flag, slots, masks
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_levels, 0xFF, l.off_orders - l.off_levels, s);
+  if (e == cudaSuccess && d.num_customers > 0 && d.num_markets > 0)
+    e = cudaMemsetAsync(mk->portfolios, 0, (size_t)d.num_markets * d.num_customers * 8, s);
+  if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in book init: %s", cudaGetErrorString(e));
+  const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
+  if (total > 0)
+    am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(view(mk), total,
+                                                                       d.max_active_orders_per_market,
+                                                                       false, nullptr);
+  return launch_status("VecMarket constructor");
+}
+
+int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const int32_t* bid_sz,
+                            const int32_t* ask_px, const int32_t* ask_sz,
+                            const int32_t* customer_ids, int32_t base_tid, int32_t* fills,
+                            int32_t* fill_counts, int32_t* bbo_bid_px, int32_t* bbo_bid_sz,
+                            int32_t* bbo_ask_px, int32_t* bbo_ask_sz, int64_t* positions,
+                            int64_t* events, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  const am_dims& d = mk->dims;
+  if (d.num_markets > 0 && (!bid_px || !bid_sz || !ask_px || !ask_sz || !customer_ids))
+    return fail(AM_ERR_INVALID, "quote pointers must not be NULL");
+  if (d.num_markets > 0 && (!fill_counts || (!fills && d.max_active_fills_per_market > 0)))
+    return fail(AM_ERR_INVALID, "fill buffers must not be NULL");
+  const int n_bbo = (bbo_bid_px != nullptr) + (bbo_bid_sz != nullptr) + (bbo_ask_px != nullptr) +
+                    (bbo_ask_sz != nullptr);
+  if (n_bbo != 0 && n_bbo != 4)
+    return fail(AM_ERR_INVALID, "BBO outputs must be all NULL or all set");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  am::StepArgs a;
+  a.bk = view(mk);
+  a.port = mk->portfolios;
+  a.N = d.num_markets; a.L = d.max_price_levels; a.O = d.max_active_orders_per_market;
+  a.F = d.max_active_fills_per_market; a.C = d.num_customers;
+  a.bid_px = bid_px; a.bid_sz = bid_sz; a.ask_px = ask_px; a.ask_sz = ask_sz;
+  a.cids = customer_ids; a.base_tid = base_tid;
+  a.fills = fills; a.fill_counts = fill_counts;
+  a.bbp = bbo_bid_px; a.bbs = bbo_bid_sz; a.bap = bbo_ask_px; a.bas = bbo_ask_sz;
+  a.pos = reinterpret_cast<long long*>(positions);
+  a.events = reinterpret_cast<unsigned long long*>(events);
+  // num_markets == 0 gives an empty grid, which CUDA rejects as the
+  // reference's launch does (market.cu:507-528)
+  const dim3 grid(blocks_for(d.num_markets)), block(am::kBlock);
+  cudaStream_t s = as_stream(stream);
+  const int variant = (n_bbo ? 1 : 0) | (positions ? 2 : 0) | (events ? 4 : 0);
+  switch (variant) {
+    case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
+    case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
+    case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
+    case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
+    case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
+    case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
+    case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
+    default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
+  }
+  return launch_status("AddTwoSidedQuotes");
+}
+
+int am_get_bbos(const am_market* mk, int32_t* bbp, int32_t* bbs, int32_t* bap, int32_t* bas,
+                void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  if (mk->dims.num_markets > 0 && (!bbp || !bbs || !bap || !bas))
+    return fail(AM_ERR_INVALID, "BBO outputs must not be NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  const am_dims& d = mk->dims;
+  am::bbo_kernel<<<blocks_for(d.num_markets), am::kBlock, 0, as_stream(stream)>>>(
+      view(mk), d.num_markets, d.max_price_levels, d.max_active_orders_per_market, bbp, bbs, bap, bas);
+  return launch_status("GetBBOs");
+}
+
+int am_update_last_prices(int32_t device, int32_t num_markets, int32_t max_fills,
+                          int32_t* last_prices, const int32_t* fill_counts, const int32_t* fills,
+                          void* stream) {
+  if (num_markets < 0 || max_fills < 0)
+    return fail(AM_ERR_INVALID, "sizes must be non-negative (N=%d F=%d)", num_markets, max_fills);
+  if (num_markets > 0 && (!last_prices || !fill_counts || (!fills && max_fills > 0)))
+    return fail(AM_ERR_INVALID, "buffers must not be NULL");
+  if (num_markets == 0) return ok();
+  DeviceGuard g(device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(g.err));
+  am::last_price_kernel<<<blocks_for(num_markets), am::kBlock, 0, as_stream(stream)>>>(
+      num_markets, max_fills, last_prices, fill_counts, fills);
+  return launch_status("UpdateLastPrices");
+}
+
+int am_reset(const am_market* mk, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  const am_dims& d = mk->dims;
+  const am::Layout l = am::layout_of(d.num_markets, d.max_price_levels, d.max_active_orders_per_market);
+  char* b = static_cast<char*>(mk->book);
+  cudaStream_t s = as_stream(stream);
+  // slots + masks = 0, levels = -1 (market.cu:699-709); the flag is kept
+  cudaError_t e = cudaMemsetAsync(b + l.off_slots, 0, l.off_levels - l.off_slots, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_levels, 0xFF, l.off_orders - l.off_levels, s);
+  if (e == cudaSuccess && d.num_customers > 0 && d.num_markets > 0)
+    e = cudaMemsetAsync(mk->portfolios, 0, (size_t)d.num_markets * d.num_customers * 8, s);
+  if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in Reset: %s", cudaGetErrorString(e));
+  const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
+  if (total > 0)
+    am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(
+        view(mk), total, d.max_active_orders_per_market, true, nullptr);
+  return launch_status("Reset");
+}
+
+int am_clear_quotes(const am_market* mk, const uint8_t* mask, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  const am_dims& d = mk->dims;
+  if (d.num_markets == 0) return ok();
+  if (!mask) return fail(AM_ERR_INVALID, "reset_indices is NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  cudaStream_t s = as_stream(stream);
+  const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
+  am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(
+      view(mk), total, d.max_active_orders_per_market, true, mask);
+  int rc2 = launch_status("ClearQuotes");
+  if (rc2) return rc2;
+  const int64_t lv = (int64_t)d.num_markets * d.max_price_levels * 2;
+  am::clear_levels_kernel<<<grid_stride_blocks(lv > d.num_markets ? lv : d.num_markets), am::kBlock, 0, s>>>(
+      view(mk), d.num_markets, d.max_price_levels, mask);
+  return launch_status("ClearQuotes");
+}
+
+int am_export_state(const am_market* mk, int32_t market0, int32_t count, int32_t* bid_heads,
+                    int32_t* bid_tails, int32_t* ask_heads, int32_t* ask_tails,
+                    int32_t* order_prices, int32_t* order_sizes, int32_t* order_customer_ids,
+                    int32_t* order_tid, uint8_t* order_is_bid, int32_t* order_next,
+                    int32_t* order_next_slots, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  const am_dims& d = mk->dims;
+  if ((rc = check_range(d, market0, count))) return rc;
+  if (count == 0) return ok();
+  if (!bid_heads || !bid_tails || !ask_heads || !ask_tails || !order_prices || !order_sizes ||
+      !order_customer_ids || !order_tid || !order_is_bid || !order_next || !order_next_slots)
+    return fail(AM_ERR_INVALID, "state buffers must not be NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  am::RefState r{bid_heads, bid_tails, ask_heads, ask_tails, order_prices, order_sizes,
+                 order_customer_ids, order_tid, order_is_bid, order_next, order_next_slots};
+  const int64_t n = (int64_t)count * (d.max_active_orders_per_market > d.max_price_levels
+                                          ? d.max_active_orders_per_market
+                                          : d.max_price_levels);
+  am::export_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(
+      view(mk), market0, count, d.max_price_levels, d.max_active_orders_per_market, r);
+  return launch_status("export_state");
+}
+
+int am_import_state(const am_market* mk, int32_t market0, int32_t count,
+                    const int32_t* bid_heads, const int32_t* bid_tails, const int32_t* ask_heads,
+                    const int32_t* ask_tails, const int32_t* order_prices,
+                    const int32_t* order_sizes, const int32_t* order_customer_ids,
+                    const int32_t* order_tid, const uint8_t* order_is_bid,
+                    const int32_t* order_next, const int32_t* order_next_slots, void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  const am_dims& d = mk->dims;
+  if ((rc = check_range(d, market0, count))) return rc;
+  if (count == 0) return ok();
+  if (!bid_heads || !bid_tails || !ask_heads || !ask_tails || !order_prices || !order_sizes ||
+      !order_customer_ids || !order_tid || !order_is_bid || !order_next || !order_next_slots)
+    return fail(AM_ERR_INVALID, "state buffers must not be NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  am::RefState r{const_cast<int32_t*>(bid_heads), const_cast<int32_t*>(bid_tails),
+                 const_cast<int32_t*>(ask_heads), const_cast<int32_t*>(ask_tails),
+                 const_cast<int32_t*>(order_prices), const_cast<int32_t*>(order_sizes),
+                 const_cast<int32_t*>(order_customer_ids), const_cast<int32_t*>(order_tid),
+                 const_cast<uint8_t*>(order_is_bid), const_cast<int32_t*>(order_next),
+                 const_cast<int32_t*>(order_next_slots)};
+  const int64_t n = (int64_t)count * (d.max_active_orders_per_market > d.max_price_levels
+                                          ? d.max_active_orders_per_market
+                                          : d.max_price_levels);
+  am::import_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(
+      view(mk), d.num_markets, market0, count, d.max_price_levels,
+      d.max_active_orders_per_market, r);
+  return launch_status("import_state");
+}
+
+int am_check_state(const am_market* mk, void* stream, int32_t* flag_out) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  cudaStream_t s = as_stream(stream);
+  int32_t flag = 0;
+  cudaError_t e = cudaMemcpyAsync(&flag, mk->book, sizeof flag, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && flag != 0) e = cudaMemsetAsync(mk->book, 0, sizeof flag, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in check_state: %s", cudaGetErrorString(e));
+  if (flag_out) *flag_out = flag;
+  if (flag != 0)
+    return fail(AM_ERR_STATE, "book state check failed (flag 0x%x: %s%s%s)", flag,
+                (flag & am::kBadSlot) ? "slot/link out of range " : "",
+                (flag & am::kBadLevel) ? "occupied level without a head " : "",
+                (flag & am::kBadImport) ? "imported value out of range" : "");
+  return ok();
+}
+
+int am_generate_quotes(int32_t device, const am_quote_gen* gen, uint32_t step0, uint32_t nsteps,
+                       int64_t market0, int32_t n, int32_t* mid_state, int32_t* out,
+                       void* stream) {
+  if (!gen) return fail(AM_ERR_INVALID, "gen is NULL");
+  if (n < 0 || market0 < 0) return fail(AM_ERR_INVALID, "n and market0 must be non-negative");
+  if (gen->cid_cycle < 1) return fail(AM_ERR_INVALID, "cid_cycle >= 1 (cid_cycle = %d)", gen->cid_cycle);
+  if (n == 0 || nsteps == 0) return ok();
+  if (!mid_state || !out) return fail(AM_ERR_INVALID, "buffers must not be NULL");
+  DeviceGuard g(device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(g.err));
+  am::quotegen_kernel<<<blocks_for(n), am::kBlock, 0, as_stream(stream)>>>(*gen, step0, nsteps,
+                                                                           market0, n, mid_state, out);
+  return launch_status("generate_quotes");
+}
+
+}  // extern "C"

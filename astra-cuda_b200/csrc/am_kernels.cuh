@@ -1,0 +1,387 @@
+// Matching-engine kernels for sm_100a.
+//
+// One thread owns one market for the whole step (quotes -> inserts -> match
+// loop -> epilogue).  The per-market work is a short chain of dependent
+// memory accesses, so throughput comes from having many markets in flight per
+// SM (memory-level parallelism), not from splitting one market across lanes.
+// The level scans of the reference (market.cu:127-142, 248-271, 298-319) are
+// replaced by 128-bit occupancy masks searched with __clzll/__ffsll in
+// registers; the masks are read and written coalesced once per step.
+#pragma once
+
+#include "am_device.cuh"
+#include "am_quotegen.cuh"
+
+namespace am {
+
+struct StepArgs {
+  BookView bk;
+  int32_t* port;  // [N][C][2]
+  int N, L, O, F, C;
+  const int32_t *bid_px, *bid_sz, *ask_px, *ask_sz, *cids;
+  int32_t base_tid;
+  int32_t* fills;       // [N][F][8]
+  int32_t* fill_counts; // [N]
+  int32_t *bbp, *bbs, *bap, *bas;
+  long long* pos;       // [N][C][2] int64 or null
+  unsigned long long* events;  // [5] or null
+};
+
+// Adds one order to side `side` (0 bid, 1 ask) at level `px`; `e` is that
+// level's entry, loaded by the caller.  Restates add_orders_kernel
+// (market.cu:45-69 / :74-98): take slot = counter++ % O, write the record
+// with no successor, append it to the level's FIFO.
+__device__ __forceinline__ void insert_order(const StepArgs& a, int4* rec, uint32_t* lv,
+                                             int side, int px, int sz, int cid, int tid,
+                                             int& ns, uint32_t& e, Mask128& mask) {
+  const int slot = (int)((uint32_t)ns % (uint32_t)a.O);
+  ns = wadd(ns, 1);
+  st_rec(rec + slot, make_int4(sz, cid, tid, make_meta(-1, px, side == 0 ? 1 : 0)));
+  const int old_tail = lv_tail(e);
+  if (old_tail == -1) {
+    e = lv_make(slot, slot);
+    mset(mask, px);
+  } else {
+    e = lv_make(lv_head(e), slot);
+    if ((uint32_t)old_tail < (uint32_t)a.O) st_rec_next(rec + old_tail, slot);
+    else flag_state(a.bk.flag, kBadSlot);
+  }
+  lv[2 * px + side] = e;
+}
+
+template <bool kBBO, bool kPos, bool kEvents>
+__global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  int e_ins = 0, e_fill = 0, e_rm = 0, e_empty = 0;
+  unsigned long long touched = 0;
+  if (m < a.N) {
+    const size_t N = (size_t)a.N;
+    const int L = a.L, O = a.O, F = a.F, C = a.C;
+    const int bp = ld_stream(a.bid_px + m), bs = ld_stream(a.bid_sz + m);
+    const int ap = ld_stream(a.ask_px + m), as = ld_stream(a.ask_sz + m);
+    const int cid = ld_stream(a.cids + m);
+    int ns = a.bk.slots[m];
+    Mask128 bm{a.bk.mask[m], a.bk.mask[N + m]};
+    Mask128 am_{a.bk.mask[2 * N + m], a.bk.mask[3 * N + m]};
+    uint32_t* lv = a.bk.levels + (size_t)m * (size_t)L * 2;
+    int4* rec = a.bk.orders + (size_t)m * (size_t)O;
+
+    // market.cu:44 / :73 -- a negative price is undefined there; not added here
+    const bool add_b = bs > 0 && bp < L && bp >= 0;
+    const bool add_a = as > 0 && ap < L && ap >= 0;
+    // both level entries are independent: issue the loads together
+    uint32_t eb = add_b ? lv[2 * bp] : kEmptyLevel;
+    uint32_t ea = add_a ? lv[2 * ap + 1] : kEmptyLevel;
+    int eb_lvl = -2, ea_lvl = -2;  // level whose entry eb / ea holds
+    if (add_b) {
+      insert_order(a, rec, lv, 0, bp, bs, cid, a.base_tid, ns, eb, bm);
+      eb_lvl = bp;
+      ++e_ins;
+    }
+    if (add_a) {
+      insert_order(a, rec, lv, 1, ap, as, cid, wadd(a.base_tid, 1), ns, ea, am_);
+      ea_lvl = ap;
+      ++e_ins;
+    }
+
+    // match_orders_kernel, market.cu:120-274
+    int bb = mhigh(bm), ba = mlow(am_, L);
+    int fc = 0;
+    while (bb >= 0 && ba < L && bb >= ba) {
+      if (eb_lvl != bb) { eb = lv[2 * bb]; eb_lvl = bb; }
+      if (ea_lvl != ba) { ea = lv[2 * ba + 1]; ea_lvl = ba; }
+      const int bslot = lv_head(eb), aslot = lv_head(ea);
+      if (bslot == -1 || aslot == -1) break;  // market.cu:155
+      if ((uint32_t)bslot >= (uint32_t)O || (uint32_t)aslot >= (uint32_t)O) {
+        flag_state(a.bk.flag, kBadSlot);
+        break;
+      }
+      const int4 B = ld_rec(rec + bslot);  // {size, cid, tid, meta}
+      const int4 A = ld_rec(rec + aslot);
+      const bool bid_is_quote = B.z < A.z;  // market.cu:172
+      const int price = bid_is_quote ? meta_price(B.w) : meta_price(A.w);
+      const int q = min(B.x, A.x);
+      if (fc >= F) { fc = -1; break; }  // market.cu:187-195
+      int4* fr = reinterpret_cast<int4*>(a.fills + ((size_t)m * (size_t)F + (size_t)fc) * 8);
+      // {price, size, taker cid, quoter cid} {quote size, taker tid, quote tid, is_sell_quote}
+      st_stream_v4(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y));
+      st_stream_v4(fr + 1, make_int4(bid_is_quote ? B.x : A.x, bid_is_quote ? A.z : B.z,
+                                     bid_is_quote ? B.z : A.z, bid_is_quote ? 0 : 1));
+      // portfolios, market.cu:221-232 (buyer = bid's customer, seller = ask's)
+      if ((uint32_t)B.y < (uint32_t)C && (uint32_t)A.y < (uint32_t)C && B.y != A.y) {
+        const int notional = wmul(price, q);
+        int2* pb = reinterpret_cast<int2*>(a.port + ((size_t)m * C + B.y) * 2);
+        int2* pa = reinterpret_cast<int2*>(a.port + ((size_t)m * C + A.y) * 2);
+        int2 vb = *pb, va = *pa;
+        vb.x = wadd(vb.x, q); vb.y = wsub(vb.y, notional);
+        va.x = wsub(va.x, q); va.y = wadd(va.y, notional);
+        *pb = vb; *pa = va;
+      }  // same customer on both sides: +q-q and -n+n leave it unchanged
+      if (kPos && B.y != A.y) {
+        const long long n64 = (long long)price * (long long)q;
+        if ((uint32_t)B.y < (uint32_t)C) {
+          longlong2* p = reinterpret_cast<longlong2*>(a.pos + ((size_t)m * C + B.y) * 2);
+          longlong2 v = *p; v.x += q; v.y -= n64; *p = v;
+        }
+        if ((uint32_t)A.y < (uint32_t)C) {
+          longlong2* p = reinterpret_cast<longlong2*>(a.pos + ((size_t)m * C + A.y) * 2);
+          longlong2 v = *p; v.x -= q; v.y += n64; *p = v;
+        }
+      }
+      if (kEvents) {
+        ++e_fill;
+        if ((uint32_t)B.y < 64u && B.y < C) touched |= 1ull << B.y;
+        if ((uint32_t)A.y < 64u && A.y < C) touched |= 1ull << A.y;
+      }
+      ++fc;
+      // market.cu:237-238: both sizes drop by q (twice when one record heads both sides)
+      int nb, na;
+      if (bslot == aslot) {
+        nb = na = wsub(wsub(B.x, q), q);
+        st_rec_size(rec + bslot, nb);
+      } else {
+        nb = wsub(B.x, q);
+        na = wsub(A.x, q);
+        st_rec_size(rec + bslot, nb);
+        st_rec_size(rec + aslot, na);
+      }
+      if (nb == 0) {  // market.cu:241-256
+        const int nx = meta_next(B.w);
+        ++e_rm;
+        if (nx == -1) {
+          eb = kEmptyLevel;
+          lv[2 * bb] = eb;
+          mclr(bm, bb);
+          bb = mhigh(bm);
+          eb_lvl = -2;
+          ++e_empty;
+        } else {
+          eb = lv_make(nx, lv_tail(eb));
+          lv[2 * bb] = eb;
+        }
+      }
+      if (na == 0) {  // market.cu:258-273
+        const int nx = meta_next(A.w);
+        ++e_rm;
+        if (nx == -1) {
+          ea = kEmptyLevel;
+          lv[2 * ba + 1] = ea;
+          mclr(am_, ba);
+          ba = mlow(am_, L);
+          ea_lvl = -2;
+          ++e_empty;
+        } else {
+          ea = lv_make(nx, lv_tail(ea));
+          lv[2 * ba + 1] = ea;
+        }
+      }
+    }
+    a.bk.slots[m] = ns;
+    a.bk.mask[m] = bm.lo;
+    a.bk.mask[N + m] = bm.hi;
+    a.bk.mask[2 * N + m] = am_.lo;
+    a.bk.mask[3 * N + m] = am_.hi;
+    st_stream(a.fill_counts + m, fc);  // market.cu:277 (or -1 from :193)
+
+    if (kBBO) {  // get_bbo_kernel on the post-match book, market.cu:291-319
+      int obp = -1, obs = 0, oap = -1, oas = 0;
+      if (bb >= 0) {
+        if (eb_lvl != bb) eb = lv[2 * bb];
+        const int h = lv_head(eb);
+        if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
+        else flag_state(a.bk.flag, kBadLevel);
+      }
+      if (ba < L) {
+        if (ea_lvl != ba) ea = lv[2 * ba + 1];
+        const int h = lv_head(ea);
+        if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
+        else flag_state(a.bk.flag, kBadLevel);
+      }
+      st_stream(a.bbp + m, obp);
+      st_stream(a.bbs + m, obs);
+      st_stream(a.bap + m, oap);
+      st_stream(a.bas + m, oas);
+    }
+  }
+  if (kEvents) {
+    int e_touch = __popcll(touched);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      e_ins += __shfl_xor_sync(0xFFFFFFFFu, e_ins, o);
+      e_fill += __shfl_xor_sync(0xFFFFFFFFu, e_fill, o);
+      e_rm += __shfl_xor_sync(0xFFFFFFFFu, e_rm, o);
+      e_empty += __shfl_xor_sync(0xFFFFFFFFu, e_empty, o);
+      e_touch += __shfl_xor_sync(0xFFFFFFFFu, e_touch, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(a.events + 0, (unsigned long long)e_ins);
+      atomicAdd(a.events + 1, (unsigned long long)e_fill);
+      atomicAdd(a.events + 2, (unsigned long long)e_rm);
+      atomicAdd(a.events + 3, (unsigned long long)e_empty);
+      atomicAdd(a.events + 4, (unsigned long long)e_touch);
+    }
+  }
+}
+
+// get_bbo_kernel (market.cu:280-320) from the occupancy masks.
+__global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, int O,
+                                                     int32_t* bbp, int32_t* bbs, int32_t* bap,
+                                                     int32_t* bas) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= N) return;
+  const size_t n = (size_t)N;
+  const Mask128 bm{bk.mask[m], bk.mask[n + m]}, am_{bk.mask[2 * n + m], bk.mask[3 * n + m]};
+  const int bb = mhigh(bm), ba = mlow(am_, L);
+  const uint32_t* lv = bk.levels + (size_t)m * (size_t)L * 2;
+  const int4* rec = bk.orders + (size_t)m * (size_t)O;
+  const uint32_t eb = bb >= 0 ? lv[2 * bb] : kEmptyLevel;
+  const uint32_t ea = ba < L ? lv[2 * ba + 1] : kEmptyLevel;
+  int obp = -1, obs = 0, oap = -1, oas = 0;
+  if (bb >= 0) {
+    const int h = lv_head(eb);
+    if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
+    else flag_state(bk.flag, kBadLevel);
+  }
+  if (ba < L) {
+    const int h = lv_head(ea);
+    if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
+    else flag_state(bk.flag, kBadLevel);
+  }
+  st_stream(bbp + m, obp);
+  st_stream(bbs + m, obs);
+  st_stream(bap + m, oap);
+  st_stream(bas + m, oas);
+}
+
+// update_last_prices_kernel (market.cu:767-786) on the packed fill records.
+__global__ void __launch_bounds__(kBlock) last_price_kernel(int N, int F, int32_t* last,
+                                                            const int32_t* counts,
+                                                            const int32_t* fills) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= N) return;
+  const int c = counts[m];
+  if (c > 0 && c <= F) last[m] = fills[((size_t)m * (size_t)F + (size_t)(c - 1)) * 8];
+}
+
+// Constructor / Reset state of the order records: a record is zero except
+// its link (-1) -- market.cu:368-373.  With keep_fields, only the link is
+// cleared (Reset, market.cu:706, and ClearQuotes, :744-745, for masked markets).
+__global__ void records_kernel(BookView bk, int64_t total, int O, bool keep_fields,
+                               const uint8_t* mask) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (mask && !mask[i / O]) continue;
+    if (keep_fields) st_rec_next(bk.orders + i, -1);
+    else st_rec(bk.orders + i, make_int4(0, 0, 0, make_meta(-1, 0, 0)));
+  }
+}
+
+// ClearQuotes for levels, slot counters and masks of masked markets.
+__global__ void clear_levels_kernel(BookView bk, int N, int L, const uint8_t* mask) {
+  const int64_t total = (int64_t)N * L * 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / (2 * (int64_t)L);
+    if (mask[m]) bk.levels[i] = kEmptyLevel;
+  }
+  for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < N;
+       m += (int64_t)gridDim.x * blockDim.x) {
+    if (!mask[m]) continue;
+    bk.slots[m] = 0;
+    for (int w = 0; w < 4; ++w) bk.mask[w * (size_t)N + m] = 0ull;
+  }
+}
+
+struct RefState {
+  int32_t *bid_heads, *bid_tails, *ask_heads, *ask_tails;
+  int32_t *prices, *sizes, *cids, *tids;
+  uint8_t* is_bid;
+  int32_t *next, *next_slots;
+};
+
+// Book -> reference layout for markets [m0, m0+count); outputs are indexed
+// from market m0.
+__global__ void export_kernel(BookView bk, int m0, int count, int L, int O, RefState r) {
+  const int64_t n_rec = (int64_t)count * O, n_lv = (int64_t)count * L;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int4* orders = bk.orders + (size_t)m0 * O;
+  const uint32_t* levels = bk.levels + (size_t)m0 * L * 2;
+  for (int64_t i = t0; i < n_rec; i += stride) {
+    const int4 v = orders[i];
+    r.sizes[i] = v.x; r.cids[i] = v.y; r.tids[i] = v.z;
+    r.next[i] = meta_next(v.w); r.prices[i] = meta_price(v.w);
+    r.is_bid[i] = (uint8_t)meta_is_bid(v.w);
+  }
+  for (int64_t i = t0; i < n_lv; i += stride) {
+    const uint32_t eb = levels[2 * i], ea = levels[2 * i + 1];
+    r.bid_heads[i] = lv_head(eb); r.bid_tails[i] = lv_tail(eb);
+    r.ask_heads[i] = lv_head(ea); r.ask_tails[i] = lv_tail(ea);
+  }
+  for (int64_t j = t0; j < count; j += stride) r.next_slots[j] = bk.slots[m0 + j];
+}
+
+__device__ __forceinline__ bool slot_ok(int v, int O) { return v >= -1 && v < O; }
+
+// Reference layout -> book for markets [m0, m0+count); masks are rebuilt
+// from the heads.  N is the book's market count (the mask stride).
+__global__ void import_kernel(BookView bk, int N, int m0, int count, int L, int O, RefState r) {
+  const int64_t n_rec = (int64_t)count * O, n_lv = (int64_t)count * L;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  int4* orders = bk.orders + (size_t)m0 * O;
+  uint32_t* levels = bk.levels + (size_t)m0 * L * 2;
+  for (int64_t i = t0; i < n_rec; i += stride) {
+    const int nx = r.next[i], px = r.prices[i], ib = r.is_bid[i] ? 1 : 0;
+    if (!slot_ok(nx, O) || px < 0 || px > 255) flag_state(bk.flag, kBadImport);
+    orders[i] = make_int4(r.sizes[i], r.cids[i], r.tids[i],
+                          make_meta(slot_ok(nx, O) ? nx : -1, px & 0xFF, ib));
+  }
+  for (int64_t i = t0; i < n_lv; i += stride) {
+    int bh = r.bid_heads[i], bt = r.bid_tails[i], ah = r.ask_heads[i], at = r.ask_tails[i];
+    if (!slot_ok(bh, O) || !slot_ok(bt, O) || !slot_ok(ah, O) || !slot_ok(at, O)) {
+      flag_state(bk.flag, kBadImport);
+      bh = slot_ok(bh, O) ? bh : -1; bt = slot_ok(bt, O) ? bt : -1;
+      ah = slot_ok(ah, O) ? ah : -1; at = slot_ok(at, O) ? at : -1;
+    }
+    levels[2 * i] = lv_make(bh, bt);
+    levels[2 * i + 1] = lv_make(ah, at);
+  }
+  for (int64_t j = t0; j < count; j += stride) {
+    const int s = r.next_slots[j];
+    if (s < 0) flag_state(bk.flag, kBadImport);
+    const size_t m = (size_t)m0 + (size_t)j;
+    bk.slots[m] = s < 0 ? 0 : s;
+    Mask128 bm{0, 0}, am_{0, 0};
+    for (int p = 0; p < L; ++p) {
+      if (r.bid_heads[(size_t)j * L + p] != -1) mset(bm, p);
+      if (r.ask_heads[(size_t)j * L + p] != -1) mset(am_, p);
+    }
+    bk.mask[m] = bm.lo; bk.mask[(size_t)N + m] = bm.hi;
+    bk.mask[2 * (size_t)N + m] = am_.lo; bk.mask[3 * (size_t)N + m] = am_.hi;
+  }
+}
+
+__global__ void __launch_bounds__(kBlock) quotegen_kernel(am_quote_gen g, uint32_t step0,
+                                                          uint32_t nsteps, int64_t market0,
+                                                          int n, int32_t* mid_state,
+                                                          int32_t* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int32_t mid = mid_state[i];
+  const uint32_t gm = (uint32_t)(market0 + i);
+  const int cid_cycle = g.cid_cycle > 0 ? g.cid_cycle : 1;
+  for (uint32_t s = 0; s < nsteps; ++s) {
+    const uint32_t t = step0 + s;
+    const Quote q = gen_quote(g, t, gm, mid);
+    int32_t* o = out + (size_t)s * 5 * (size_t)n;
+    o[i] = q.bid_px;
+    o[(size_t)n + i] = q.bid_sz;
+    o[2 * (size_t)n + i] = q.ask_px;
+    o[3 * (size_t)n + i] = q.ask_sz;
+    o[4 * (size_t)n + i] = (int32_t)(t % (uint32_t)cid_cycle);
+  }
+  mid_state[i] = mid;
+}
+
+}  // namespace am

@@ -1,0 +1,433 @@
+"""Benchmark of the matching step: market-steps/s and step latency.
+
+Workload (default --config 4, the trading-game rollout shape): 1M markets per
+GPU, 128 price levels, 512-slot order ring, 512 fill slots, 5 customers
+rotating one quote per step, GetBBOs every step and int64 per-customer
+position/cash reduced from the fills every step.  A step is one call of
+``VecMarket.add_two_sided_quotes(..., bbos=, positions=)`` over every market
+(one fused launch).  Quotes are the seeded synthetic stream of
+``astra_cuda.workloads`` (seed 0), drawn on the device by global market id.
+
+The run covers steps [0, S) with S = max(config steps, W + K): steps before
+S-K-W are an untimed pre-roll that brings the book to the configuration's
+state, the next W are the warm-up, the last K are timed.  Per-step CUDA events
+on the launching stream give the step times; the timed region is bracketed by
+a barrier and a device synchronise and its time is the max over ranks.
+
+Also reported on the same line:
+* ``e2e`` -- the same metric through the public API with the quotes in pinned
+  host memory, copied in every step, and each step's fill counts copied back;
+* ``roofline`` -- algorithmic bytes of the timed steps (event totals counted
+  by a replay of the same steps from a snapshot) over the mean step time,
+  against the measured HBM copy bandwidth;
+* ``cpu_baseline`` -- the CPU restatement of the reference's kernels (OpenMP
+  over markets) timed on a sample of the same workload, rank 0, N = 1 only;
+* ``unfused`` -- the same steps with GetBBOs as its own launch, the call
+  pattern of the reference's API;
+* ``gather`` (N > 1) -- NCCL gather of BBOs and positions to rank 0, timed
+  separately from matching.
+
+``--impl reference`` times the reference's algorithm on the host cores: the
+CPU restatement of market.cu (the reference has no CPU path of its own), on a
+sample of the same workload; rank 0 alone runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "astra-cuda_b200"))
+
+METRIC = "market-steps/sec at 1M markets, 1/2/4/8 B200; p50 step latency"
+UNIT = "market-steps/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=500)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=4)
+    ap.add_argument("--markets", type=int, default=0, help="markets per GPU (default: the config's largest)")
+    ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--cpu-sample", type=int, default=8192, help="markets in the CPU baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip unfused/e2e/replay legs")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.path = os.path.join("/tmp", f"bench_clocks_{os.getpid()}.csv")
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(gpu_index)], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_reference(args, rank):
+    """--impl reference: the CPU restatement of market.cu on host threads."""
+    if rank != 0:
+        return
+    from astra_cuda import workloads
+    cfg = workloads.CONFIGS[args.config]
+    res = cpu_baseline(cfg, args, sample=args.cpu_sample)
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "p50_step_ms": res["p50_step_ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int32",
+            "data": "synthetic", "config": config_dict(cfg, args, res["markets"], 1),
+            "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(cfg, args, sample):
+    """Times orc_step + orc_bbo (the reference's AddTwoSidedQuotes + GetBBOs,
+    restated in C, OpenMP over markets) on `sample` markets over the same
+    step window as the GPU run; quote generation is outside the timing."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+    oracle.build()
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    S = max(cfg["steps"], args.warmup + args.steps)
+    t_first = S - args.steps
+    L, O, F, C = cfg["L"], cfg["O"], cfg["F"], cfg["C"]
+    mkt = oracle.OracleMarket(sample, L, O, F, C)
+    fills, bbos = mkt.new_fill_batch(), mkt.new_bbo_batch()
+    gen = oracle.OracleQuoteGen(cfg["gen"], 0, sample)
+    pos = np.zeros((sample, C, 2), np.int64) if cfg["pos64"] else None
+    times = []
+    for t in range(S):
+        q = gen.step()
+        t0 = time.perf_counter()
+        mkt.add_two_sided_quotes(*q, fills, pos64=pos, threads=threads)
+        mkt.get_bbos(bbos, threads=threads)
+        dt = time.perf_counter() - t0
+        if t >= t_first:
+            times.append(dt)
+    tot = sum(times)
+    return {"value": sample * len(times) / tot, "unit": UNIT, "cores": threads, "kind": "port",
+            "markets": sample, "ms_per_step": 1e3 * tot / len(times),
+            "p50_step_ms": 1e3 * statistics.median(times),
+            "sample": (f"{sample} markets of config {args.config} (global ids 0..{sample - 1}), "
+                       f"steps {t_first}..{S - 1} timed after an untimed run of steps 0..{t_first - 1}; "
+                       f"AddTwoSidedQuotes + GetBBOs per step, OpenMP over markets")}
+
+
+def config_dict(cfg, args, markets, world):
+    return {"workload": f"config{args.config}:{cfg['name']}", "markets_per_gpu": markets,
+            "total_markets": markets * world, "max_price_levels": cfg["L"],
+            "max_active_orders": cfg["O"], "max_active_fills": cfg["F"],
+            "num_customers": cfg["C"], "bbo_every_step": cfg["bbo_every_step"],
+            "positions_int64": cfg["pos64"], "parallelism": f"dp{world} (market shards)",
+            "l2": "no flush: each step touches ~0.5 GB of scattered book sectors (> 126 MB L2) "
+                  "and reads fresh quotes"}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+    from astra_cuda import order_matching as aom, workloads
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    cfg = workloads.CONFIGS[args.config]
+    N = args.markets or max(cfg["markets"])
+    L, O, F, C = cfg["L"], cfg["O"], cfg["F"], cfg["C"]
+    K, W = args.steps, args.warmup
+    S = max(cfg["steps"], W + K)
+    market0 = rank * N
+
+    mkt = aom.VecMarket(N, L, O, F, C, device_id=local)
+    fills, bbos = mkt.new_fill_batch(), mkt.new_bbo_batch()
+    pos = torch.zeros((N, C, 2), dtype=torch.int64, device=dev) if cfg["pos64"] else None
+    stream = workloads.DeviceQuoteStream(cfg["gen"], market0, N, dev)
+    kw = {"bbos": bbos}
+    if pos is not None:
+        kw["positions"] = pos
+
+    def step(q):
+        mkt.add_two_sided_quotes(q[0], q[1], q[2], q[3], q[4], fills, **kw)
+
+    # pre-roll (untimed): steps [0, S-K-W)
+    pre = S - K - W
+    chunk = 64
+    t = 0
+    while t < pre:
+        k = min(chunk, pre - t)
+        q = stream.take(k)
+        for i in range(k):
+            step(q[i])
+        t += k
+    # quotes of the warm-up and timed steps, resident in HBM before timing
+    qs = stream.take(W + K)
+    for i in range(W):
+        step(qs[i])
+    torch.cuda.synchronize()
+
+    snap = mkt.clone() if not args.no_extras else None
+    snap_pos = pos.clone() if (pos is not None and snap is not None) else None
+    clocks = ClockSampler(local)
+    time.sleep(0.25)
+
+    cur = torch.cuda.current_stream(dev)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs[0].record(cur)
+    for i in range(K):
+        step(qs[W + i])
+        evs[i + 1].record(cur)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(K)]
+    total_ms = evs[0].elapsed_time(evs[K])
+    last_counts = fills.fill_counts.clone()
+
+    extras = {}
+    if snap is not None:
+        # unfused: GetBBOs as its own launch, as the reference's callers do
+        u = snap.clone()
+        ufills, ubbos = fills, u.new_bbo_batch()  # fills are reused: only counts are compared
+        upos = snap_pos.clone() if snap_pos is not None else None
+        ukw = {"positions": upos} if upos is not None else {}
+        ue = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ue[0].record(cur)
+        for i in range(K):
+            q = qs[W + i]
+            u.add_two_sided_quotes(q[0], q[1], q[2], q[3], q[4], ufills, **ukw)
+            u.get_bbos(ubbos)
+        ue[1].record(cur)
+        torch.cuda.synchronize()
+        unf_ms = ue[0].elapsed_time(ue[1]) / K
+        assert torch.equal(ufills.fill_counts, last_counts)
+        assert torch.equal(ubbos.storage[:4], bbos.storage[:4])
+        extras["unfused"] = {"ms_per_step": unf_ms, "value": N * world / (unf_ms * 1e-3),
+                             "launches_per_step": 2}
+        del u, ubbos, upos
+        # replay the timed steps with event counters for the bytes model
+        ev = torch.zeros(5, dtype=torch.int64, device=dev)
+        rkw = {"bbos": snap.new_bbo_batch(), "events": ev}
+        if snap_pos is not None:
+            rkw["positions"] = snap_pos
+        rfills = fills
+        for i in range(K):
+            q = qs[W + i]
+            snap.add_two_sided_quotes(q[0], q[1], q[2], q[3], q[4], rfills, **rkw)
+        torch.cuda.synchronize()
+        assert torch.equal(rfills.fill_counts, last_counts), "replay diverged"
+        e = [int(x) for x in ev.cpu().tolist()]
+        extras["events"] = dict(zip(("n_ins", "n_fill", "n_rm", "n_empty", "n_touch"), e))
+        del snap, rfills, rkw
+        torch.cuda.empty_cache()
+
+    # e2e: quotes from pinned host memory every step, fill counts back
+    e2e = None
+    if not args.no_extras and args.e2e_steps > 0:
+        KE = args.e2e_steps
+        hq = stream.take(KE).cpu().pin_memory()
+        dq = torch.empty((2, 5, N), dtype=torch.int32, device=dev)
+        hcounts = torch.empty((KE, N), dtype=torch.int32).pin_memory()
+        copy_s = torch.cuda.Stream(dev)
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
+        step_done = [torch.cuda.Event() for _ in range(2)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(copy_s):
+            dq[0].copy_(hq[0], non_blocking=True)
+            h2d_done[0].record(copy_s)
+        for i in range(KE):
+            b = i % 2
+            if i + 1 < KE:  # prefetch the next step's quotes while this one runs
+                with torch.cuda.stream(copy_s):
+                    if i >= 1:
+                        copy_s.wait_event(step_done[1 - b])
+                    dq[1 - b].copy_(hq[i + 1], non_blocking=True)
+                    h2d_done[1 - b].record(copy_s)
+            cur.wait_event(h2d_done[b])
+            q = dq[b]
+            step(q)
+            step_done[b].record(cur)
+            hcounts[i].copy_(fills.fill_counts, non_blocking=True)
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        if world > 1:
+            t_max = torch.tensor([el], dtype=torch.float64, device=dev)
+            dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+            el = float(t_max.item())
+        e2e = {"value": N * world * KE / el, "unit": UNIT, "h2d_bytes_per_step": 5 * 4 * N,
+               "d2h_bytes_per_step": 4 * N, "steps": KE, "ms_per_step": 1e3 * el / KE,
+               "note": "wall clock per rank (max over ranks); quotes H2D from pinned host "
+                       "memory on a copy stream, prefetching the next step; fill counts D2H"}
+        del hq, hcounts
+
+    gather = None
+    if world > 1:
+        # NCCL gather of BBO [4, N] and positions [N, C, 2] to rank 0, timed separately
+        ge = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        pieces = [bbos.storage[:4].reshape(-1).view(torch.int8)]
+        if pos is not None:
+            pieces.append(pos.reshape(-1).view(torch.int8))
+        payload = torch.cat(pieces)
+        glist = [torch.empty_like(payload) for _ in range(world)] if rank == 0 else None
+        for _ in range(2):
+            dist.gather(payload, glist, dst=0)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ge[0].record(cur)
+        reps = 5
+        for _ in range(reps):
+            dist.gather(payload, glist, dst=0)
+        ge[1].record(cur)
+        torch.cuda.synchronize()
+        gms = torch.tensor([ge[0].elapsed_time(ge[1]) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+        gather = {"ms": float(gms.item()), "bytes_per_rank": int(payload.numel()),
+                  "what": "BBO int32 [4,N] + positions int64 [N,C,2] per rank to rank 0 (NCCL gather)"}
+        del glist
+
+    clk = clocks.stop()
+
+    # max over ranks of the timed region
+    t_tot = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_tot, op=dist.ReduceOp.MAX)
+    total_ms = float(t_tot.item())
+    ms_per_step = total_ms / K
+    value = N * world * K / (total_ms * 1e-3)
+    srt = sorted(step_ms)
+
+    if rank == 0:
+        peak, peak_src = measured_peak()
+        roof = None
+        if "events" in extras:
+            e = extras["events"]
+            alg = workloads.algorithmic_bytes(N * K, L, e["n_ins"], e["n_fill"], e["n_rm"],
+                                              e["n_empty"], True, e["n_touch"], cfg["pos64"])
+            per_launch = alg / K
+            achieved = per_launch / (statistics.mean(step_ms) * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": read_traffic(N),
+                    "algorithmic_bytes_per_launch": int(per_launch),
+                    "algorithmic_bytes_per_market_step": round(per_launch / N, 2),
+                    "peak_source": peak_src, "kernel": "step_kernel<bbo,positions> (one launch per step)"}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": ms_per_step, "p50_step_ms": srt[len(srt) // 2],
+                "p99_step_ms": srt[min(len(srt) - 1, int(0.99 * len(srt)))],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int32", "data": "synthetic (seeded counter-based quote stream, seed 0)",
+                "config": dict(config_dict(cfg, args, N, world),
+                               timed_steps=[S - K, S - 1], preroll_steps=pre),
+                "gpu_launches": K, "roofline": roof, "e2e": e2e, "clocks": clk}
+        line.update({k: v for k, v in extras.items() if k != "events"})
+        if "events" in extras:
+            line["events_timed_steps"] = extras["events"]
+        if gather:
+            line["gather"] = gather
+        if world == 1 and not args.no_cpu:
+            try:
+                line["cpu_baseline"] = cpu_baseline(cfg, args, sample=args.cpu_sample)
+            except Exception as ex:  # reported, never fatal for the GPU number
+                line["cpu_baseline"] = {"error": repr(ex)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(n_markets):
+    """DRAM bytes per launch of the step kernel from the committed ncu summary
+    (profiles/step_kernel_traffic.json: bytes per market-step measured on a
+    smaller case), scaled to n_markets; None when absent."""
+    p = os.path.join(ROOT, "profiles", "step_kernel_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return int(d["dram_bytes_per_market_step"] * n_markets)
+    except Exception:
+        return None
+
+
+if __name__ == "__main__":
+    main()

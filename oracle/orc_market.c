@@ -100,8 +100,7 @@ static void match_market(const orc_book *b, const orc_fills *f, int32_t m,
     int32_t *sizes = b->order_sizes + ob, *cids = b->order_customer_ids + ob;
     int32_t *tids = b->order_tid + ob, *prices = b->order_prices + ob;
     int32_t *next = b->order_next + ob;
-    uint64_t touched[16]; /* distinct customers touched, for the bytes model */
-    memset(touched, 0, sizeof touched);
+    uint64_t touched = 0; /* customers in [0, min(C, 64)) touched by fills */
 
     int32_t fill_count = 0;
     int32_t best_bid = scan_best_bid(bh, L);
@@ -120,6 +119,7 @@ static void match_market(const orc_book *b, const orc_fills *f, int32_t m,
         int32_t trade_size = bid_size < ask_size ? bid_size : ask_size; /* :174 */
         if (fill_count >= F) {                                          /* :187-195 */
             f->counts[m] = -1;
+            if (ev) ev->n_touch += __builtin_popcountll(touched);
             return;
         }
         size_t fi = (size_t)m * F + (size_t)fill_count;                 /* :198-218 */
@@ -152,8 +152,8 @@ static void match_market(const orc_book *b, const orc_fills *f, int32_t m,
         pos64_apply(pos64, b, m, bid_cust, ask_cust, trade_price, trade_size);
         if (ev) {
             ev->n_fill++;
-            if (bid_cust >= 0 && bid_cust < 1024) touched[bid_cust >> 6] |= 1ull << (bid_cust & 63);
-            if (ask_cust >= 0 && ask_cust < 1024) touched[ask_cust >> 6] |= 1ull << (ask_cust & 63);
+            if (bid_cust >= 0 && bid_cust < C && bid_cust < 64) touched |= 1ull << bid_cust;
+            if (ask_cust >= 0 && ask_cust < C && ask_cust < 64) touched |= 1ull << ask_cust;
         }
         fill_count++;                                                   /* :234 */
         sizes[bid_slot] = w_sub(sizes[bid_slot], trade_size);           /* :237-238 */
@@ -178,9 +178,7 @@ static void match_market(const orc_book *b, const orc_fills *f, int32_t m,
         }
     }
     f->counts[m] = fill_count;                                          /* :277 */
-    if (ev) {
-        for (int i = 0; i < 16; ++i) ev->n_touch += __builtin_popcountll(touched[i]);
-    }
+    if (ev) ev->n_touch += __builtin_popcountll(touched);
 }
 
 void orc_step(const orc_book *b, const orc_fills *f,

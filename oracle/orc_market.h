@@ -61,7 +61,7 @@ typedef struct orc_events {
     int64_t n_fill;   /* fills written */
     int64_t n_rm;     /* orders removed because their size reached 0 */
     int64_t n_empty;  /* price levels emptied by a removal */
-    int64_t n_touch;  /* distinct (market, customer) pairs touched by fills, per call */
+    int64_t n_touch;  /* per market: distinct customers in [0, min(C,64)) touched by fills */
 } orc_events;
 
 /* Constructor state (market.cu:361-380): heads/tails/next = -1, rest 0. */

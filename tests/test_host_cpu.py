@@ -1,0 +1,94 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+symbol its header declares, argument validation raises like the reference,
+the workload definitions and the bytes model hold together, and the fill
+record views map onto the right record words."""
+import ctypes
+
+import pytest
+import torch
+
+
+def test_library_exports_every_header_symbol():
+    from astra_cuda import _native
+    lib = _native.lib()
+    names = _native.header_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.am_abi_version() == 1
+
+
+def test_native_dims_validation_without_gpu():
+    from astra_cuda import _native
+    lib = _native.lib()
+    D = _native.Dims
+    assert lib.am_validate_dims(ctypes.byref(D(10, 128, 1024, 1024, 16))) == 0
+    for bad in (D(2048 * 2048 + 1, 128, 1024, 1024, 16), D(10, 129, 1024, 1024, 16),
+                D(10, 128, 1025, 1024, 16), D(10, 128, 1024, 1025, 16),
+                D(10, 128, 1024, 1024, 1025), D(10, 128, 0, 16, 16), D(-1, 128, 16, 16, 16)):
+        assert lib.am_validate_dims(ctypes.byref(bad)) == _native.AM_ERR_INVALID
+        assert _native.last_error()
+    nbytes = ctypes.c_uint64(0)
+    assert lib.am_book_bytes(ctypes.byref(D(1000, 128, 512, 512, 5)), ctypes.byref(nbytes)) == 0
+    # 16 B per order slot, 8 B per level, 36 B per market, 256-byte aligned blocks
+    assert 1000 * (16 * 512 + 8 * 128 + 36) <= nbytes.value <= 1000 * (16 * 512 + 8 * 128 + 36) + 1280
+
+
+def test_null_and_range_errors_without_gpu():
+    from astra_cuda import _native
+    lib = _native.lib()
+    assert lib.am_add_two_sided_quotes(None, *([None] * 5), 0, *([None] * 8), None) == _native.AM_ERR_INVALID
+    mk = _native.Market(_native.Dims(4, 16, 8, 8, 2), 0, 256, 512)
+    assert lib.am_export_state(ctypes.byref(mk), 3, 2, *([None] * 11), None) == _native.AM_ERR_INVALID
+    assert "outside" in _native.last_error()
+    mk.book = 100  # misaligned
+    assert lib.am_reset(ctypes.byref(mk), None) == _native.AM_ERR_INVALID
+    assert "aligned" in _native.last_error()
+
+
+def test_vecmarket_constructor_checks_like_reference():
+    from astra_cuda import order_matching as aom
+    with pytest.raises(RuntimeError, match="num_markets <= MAX_MARKETS"):
+        aom.VecMarket(aom.MAX_MARKETS + 1, 128, 1024, 1024)
+    with pytest.raises(RuntimeError, match="max_price_levels <= PRICE_LEVELS"):
+        aom.VecMarket(10, 129, 1024, 1024)
+    with pytest.raises(RuntimeError, match="threads_per_block > 0"):
+        aom.VecMarket(10, 128, 1024, 1024, threads_per_block=0)
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="device_id < device_count"):
+            aom.VecMarket(10, 128, 1024, 1024)
+    assert (aom.MAX_MARKETS, aom.PRICE_LEVELS, aom.MAX_ACTIVE_ORDERS_PER_MARKET,
+            aom.MAX_ACTIVE_FILLS_PER_MARKET, aom.NULL_INDEX, aom.MAX_CUSTOMERS) == \
+        (4194304, 128, 1024, 1024, -1, 1024)
+    import astra_cuda
+    assert astra_cuda.__version__ == "0.0.2"
+
+
+def test_fill_record_views_on_host_tensors():
+    """FillBatch views address the record words the kernel writes."""
+    from astra_cuda import order_matching as aom
+    fb = aom.FillBatch(3, 4, torch.device("cpu"))
+    for w in range(8):
+        fb.fill_records[:, :, w] = 100 + w
+    fb.fill_records[:, :, 7] = torch.tensor([0, 1, 0, 1], dtype=torch.int32)
+    assert (fb.fill_prices == 100).all() and (fb.fill_sizes == 101).all()
+    assert (fb.fill_customer_ids == 102).all() and (fb.fill_quoter_ids == 103).all()
+    assert (fb.fill_quote_sizes == 104).all() and (fb.fill_tid == 105).all()
+    assert (fb.fill_quote_tid == 106).all()
+    assert fb.fill_is_sell_quote[0].tolist() == [False, True, False, True]
+    c = fb.clone()
+    c.fill_prices = torch.zeros((3, 4), dtype=torch.int32)
+    assert (fb.fill_prices == 100).all() and (c.fill_records[:, :, 0] == 0).all()
+    bb = aom.BBOBatch(5, torch.device("cpu"))
+    bb.best_ask_sizes = torch.arange(5, dtype=torch.int32)
+    assert bb.storage[3].tolist() == [0, 1, 2, 3, 4]
+
+
+def test_bytes_model_and_configs():
+    from astra_cuda import workloads
+    assert set(workloads.CONFIGS) == {0, 1, 2, 3, 4}
+    c4 = workloads.CONFIGS[4]
+    assert (c4["markets"], c4["O"], c4["F"], c4["C"], c4["steps"]) == ([1_000_000], 512, 512, 5, 2000)
+    b = workloads.algorithmic_bytes(1, 128, n_ins=2, n_fill=1, n_rm=1, n_empty=0,
+                                    with_bbo=True, n_touch=2, with_pos64=True)
+    assert b == 20 + 8 + 4 + 32 + 66 + 101 + 8 + 24 + 32

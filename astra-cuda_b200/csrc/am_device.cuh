@@ -139,6 +139,14 @@ __device__ __forceinline__ void st_stream_v4(int4* p, int4 v) {
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
+// fire-and-forget adds (RED): the issuing thread does not wait for them
+__device__ __forceinline__ void red_add(int* p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add64(long long* p, long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ void flag_state(int32_t* flag, int code) { atomicOr(flag, code); }
 
 // state-check codes (OR-ed into the flag word)

@@ -107,25 +107,30 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       st_stream_v4(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y));
       st_stream_v4(fr + 1, make_int4(bid_is_quote ? B.x : A.x, bid_is_quote ? A.z : B.z,
                                      bid_is_quote ? B.z : A.z, bid_is_quote ? 0 : 1));
-      // portfolios, market.cu:221-232 (buyer = bid's customer, seller = ask's)
+      // portfolios, market.cu:221-232 (buyer = bid's customer, seller = ask's).
+      // One thread owns the market, so the read-modify-writes need no
+      // atomicity; they are issued as fire-and-forget reductions (RED) so the
+      // match loop never waits for them.  int32 adds wrap like the reference's.
       if ((uint32_t)B.y < (uint32_t)C && (uint32_t)A.y < (uint32_t)C && B.y != A.y) {
         const int notional = wmul(price, q);
-        int2* pb = reinterpret_cast<int2*>(a.port + ((size_t)m * C + B.y) * 2);
-        int2* pa = reinterpret_cast<int2*>(a.port + ((size_t)m * C + A.y) * 2);
-        int2 vb = *pb, va = *pa;
-        vb.x = wadd(vb.x, q); vb.y = wsub(vb.y, notional);
-        va.x = wsub(va.x, q); va.y = wadd(va.y, notional);
-        *pb = vb; *pa = va;
+        int* pb = a.port + ((size_t)m * C + B.y) * 2;
+        int* pa = a.port + ((size_t)m * C + A.y) * 2;
+        red_add(pb, q);
+        red_add(pb + 1, wsub(0, notional));
+        red_add(pa, wsub(0, q));
+        red_add(pa + 1, notional);
       }  // same customer on both sides: +q-q and -n+n leave it unchanged
       if (kPos && B.y != A.y) {
         const long long n64 = (long long)price * (long long)q;
         if ((uint32_t)B.y < (uint32_t)C) {
-          longlong2* p = reinterpret_cast<longlong2*>(a.pos + ((size_t)m * C + B.y) * 2);
-          longlong2 v = *p; v.x += q; v.y -= n64; *p = v;
+          long long* p = a.pos + ((size_t)m * C + B.y) * 2;
+          red_add64(p, (long long)q);
+          red_add64(p + 1, -n64);
         }
         if ((uint32_t)A.y < (uint32_t)C) {
-          longlong2* p = reinterpret_cast<longlong2*>(a.pos + ((size_t)m * C + A.y) * 2);
-          longlong2 v = *p; v.x -= q; v.y += n64; *p = v;
+          long long* p = a.pos + ((size_t)m * C + A.y) * 2;
+          red_add64(p, -(long long)q);
+          red_add64(p + 1, n64);
         }
       }
       if (kEvents) {

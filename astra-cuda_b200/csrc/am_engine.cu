@@ -122,7 +122,7 @@ inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 bool use_v1() {
   static const bool v1 = [] {
     const char* e = getenv("ASTRA_STEP_KERNEL");
-    return e && e[0] == '1';
+    return !(e && e[0] == '2');
   }();
   return v1;
 }
@@ -240,6 +240,20 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
   cudaStream_t s = as_stream(stream);
   const int variant = (n_bbo ? 1 : 0) | (positions ? 2 : 0) | (events ? 4 : 0);
   if (use_v1()) {
+    static const int tpb = [] {
+      const char* e = getenv("ASTRA_STEP_BLOCK");
+      int v = e ? atoi(e) : am::kBlock;
+      return (v == 32 || v == 64 || v == 128 || v == 256) ? v : am::kBlock;
+    }();
+    static const bool l2_set = [] {
+      const char* e = getenv("ASTRA_L2_FETCH");
+      if (e) cudaDeviceSetLimit(cudaLimitMaxL2FetchGranularity, (size_t)atoi(e));
+      return true;
+    }();
+    (void)l2_set;
+    const dim3 grid2(blocks_for(d.num_markets) * (am::kBlock / tpb)), block2(tpb);
+    const dim3& grid = grid2;
+    const dim3& block = block2;
     switch (variant) {
       case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
       case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;

@@ -30,23 +30,89 @@ struct StepArgs {
 // Adds one order to side `side` (0 bid, 1 ask) at level `px`; `e` is that
 // level's entry, loaded by the caller.  Restates add_orders_kernel
 // (market.cu:45-69 / :74-98): take slot = counter++ % O, write the record
-// with no successor, append it to the level's FIFO.
-__device__ __forceinline__ void insert_order(const StepArgs& a, int4* rec, uint32_t* lv,
-                                             int side, int px, int sz, int cid, int tid,
-                                             int& ns, uint32_t& e, Mask128& mask) {
+// with no successor, append it to the level's FIFO.  Keeps the two cached
+// records (slot bc -> B, slot ac -> A) equal to memory; returns the new
+// record's slot when it became the level's head (its record is then known
+// without a load), else -1.
+__device__ __forceinline__ int insert_order(const StepArgs& a, int4* rec, uint32_t* lv, int side,
+                                            int px, int sz, int cid, int tid, int& ns,
+                                            uint32_t& e, Mask128& mask, int4& B, int& bc,
+                                            int4& A, int& ac, int4& v) {
   const int slot = (int)((uint32_t)ns % (uint32_t)a.O);
   ns = wadd(ns, 1);
-  st_rec(rec + slot, make_int4(sz, cid, tid, make_meta(-1, px, side == 0 ? 1 : 0)));
+  v = make_int4(sz, cid, tid, make_meta(-1, px, side == 0 ? 1 : 0));
+  st_rec(rec + slot, v);
+  if (bc == slot) B = v;
+  if (ac == slot) A = v;
+  int head_slot = -1;
   const int old_tail = lv_tail(e);
   if (old_tail == -1) {
     e = lv_make(slot, slot);
     mset(mask, px);
+    head_slot = slot;
   } else {
     e = lv_make(lv_head(e), slot);
-    if ((uint32_t)old_tail < (uint32_t)a.O) st_rec_next(rec + old_tail, slot);
-    else flag_state(a.bk.flag, kBadSlot);
+    if ((uint32_t)old_tail < (uint32_t)a.O) {
+      st_rec_next(rec + old_tail, slot);
+      if (bc == old_tail) B.w = make_meta(slot, meta_price(B.w), meta_is_bid(B.w));
+      if (ac == old_tail) A.w = make_meta(slot, meta_price(A.w), meta_is_bid(A.w));
+    } else {
+      flag_state(a.bk.flag, kBadSlot);
+    }
   }
   lv[2 * px + side] = e;
+  return head_slot;
+}
+
+// Portfolio and int64-position updates of `reps` identical fills
+// (market.cu:221-232): buyer +size / -price*size, seller the reverse, int32
+// adds wrapping like the reference's.  One thread owns the market, so the
+// read-modify-writes need no atomicity; they are fire-and-forget reductions
+// so the match loop never waits on them.
+template <bool kPos>
+__device__ __forceinline__ void book_trade(const StepArgs& a, int m, int buyer, int seller,
+                                           int price, int size, int reps) {
+  const int C = a.C;
+  if (buyer == seller) return;  // +q-q and -n+n: unchanged
+  if ((uint32_t)buyer < (uint32_t)C && (uint32_t)seller < (uint32_t)C) {
+    const int dq = wmul(size, reps), dn = wmul(wmul(price, size), reps);
+    int* pb = a.port + ((size_t)m * C + buyer) * 2;
+    int* ps = a.port + ((size_t)m * C + seller) * 2;
+    red_add(pb, dq);
+    red_add(pb + 1, wsub(0, dn));
+    red_add(ps, wsub(0, dq));
+    red_add(ps + 1, dn);
+  }
+  if (kPos) {
+    const long long q64 = (long long)size * reps, n64 = (long long)price * size * reps;
+    if ((uint32_t)buyer < (uint32_t)C) {
+      long long* p = a.pos + ((size_t)m * C + buyer) * 2;
+      red_add64(p, q64);
+      red_add64(p + 1, -n64);
+    }
+    if ((uint32_t)seller < (uint32_t)C) {
+      long long* p = a.pos + ((size_t)m * C + seller) * 2;
+      red_add64(p, -q64);
+      red_add64(p + 1, n64);
+    }
+  }
+}
+
+// Exact state of one match iteration: best levels, their head slots and the
+// head records' sizes.  An iteration reads nothing else that can change while
+// matching (record prices, customers, tids and links are fixed then; a
+// level's tail changes only when it empties, which changes a best level).
+struct Sig {
+  unsigned long long k, s;
+};
+__device__ __forceinline__ Sig make_sig(int bb, int ba, int bslot, int aslot, int bsz, int asz) {
+  return Sig{(unsigned long long)(uint32_t)bb | ((unsigned long long)(uint32_t)ba << 8) |
+                 ((unsigned long long)(uint32_t)bslot << 16) |
+                 ((unsigned long long)(uint32_t)aslot << 40),
+             (unsigned long long)(uint32_t)bsz | ((unsigned long long)(uint32_t)asz << 32)};
+}
+__device__ __forceinline__ bool same_sig(const Sig& x, const Sig& y) {
+  return x.k == y.k && x.s == y.s;
 }
 
 template <bool kBBO, bool kPos, bool kEvents>
@@ -56,7 +122,7 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
   unsigned long long touched = 0;
   if (m < a.N) {
     const size_t N = (size_t)a.N;
-    const int L = a.L, O = a.O, F = a.F, C = a.C;
+    const int L = a.L, O = a.O, F = a.F;
     const int bp = ld_stream(a.bid_px + m), bs = ld_stream(a.bid_sz + m);
     const int ap = ld_stream(a.ask_px + m), as = ld_stream(a.ask_sz + m);
     const int cid = ld_stream(a.cids + m);
@@ -73,13 +139,18 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
     uint32_t eb = add_b ? lv[2 * bp] : kEmptyLevel;
     uint32_t ea = add_a ? lv[2 * ap + 1] : kEmptyLevel;
     int eb_lvl = -2, ea_lvl = -2;  // level whose entry eb / ea holds
+    int4 B = make_int4(0, 0, 0, 0), A = B, v;
+    int bc = -1, ac = -1;           // slots whose records B / A hold (-1: none)
     if (add_b) {
-      insert_order(a, rec, lv, 0, bp, bs, cid, a.base_tid, ns, eb, bm);
+      const int h = insert_order(a, rec, lv, 0, bp, bs, cid, a.base_tid, ns, eb, bm, B, bc, A, ac, v);
+      if (h >= 0) { B = v; bc = h; }
       eb_lvl = bp;
       ++e_ins;
     }
     if (add_a) {
-      insert_order(a, rec, lv, 1, ap, as, cid, wadd(a.base_tid, 1), ns, ea, am_);
+      const int h = insert_order(a, rec, lv, 1, ap, as, cid, wadd(a.base_tid, 1), ns, ea, am_,
+                                 B, bc, A, ac, v);
+      if (h >= 0) { A = v; ac = h; }
       ea_lvl = ap;
       ++e_ins;
     }
@@ -87,6 +158,9 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
     // match_orders_kernel, market.cu:120-274
     int bb = mhigh(bm), ba = mlow(am_, L);
     int fc = 0;
+    Sig h1{~0ull, 0}, h2{~0ull, 0};  // signatures of the previous two iterations
+    int run = 0;                     // consecutive iterations equal to the one two before
+    int rm1 = 0, rm2 = 0;            // removals made by those two iterations
     while (bb >= 0 && ba < L && bb >= ba) {
       if (eb_lvl != bb) { eb = lv[2 * bb]; eb_lvl = bb; }
       if (ea_lvl != ba) { ea = lv[2 * ba + 1]; ea_lvl = ba; }
@@ -96,8 +170,44 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
         flag_state(a.bk.flag, kBadSlot);
         break;
       }
-      const int4 B = ld_rec(rec + bslot);  // {size, cid, tid, meta}
-      const int4 A = ld_rec(rec + aslot);
+      // head records: reuse the cached copy of a slot, load only a new head
+      if (bc != bslot) {
+        if (ac == bslot) B = A; else B = ld_rec(rec + bslot);
+        bc = bslot;
+      }
+      if (ac != aslot) {
+        if (bc == aslot) A = B; else A = ld_rec(rec + aslot);
+        ac = aslot;
+      }
+      // A run of two iterations that each repeat the one two before makes
+      // the loop periodic with period 2 from there on (period 1 included):
+      // every later iteration reads exactly what the one two before read.
+      // The remaining fills then repeat the last two; write them in bulk.
+      const Sig sg = make_sig(bb, ba, bslot, aslot, B.x, A.x);
+      run = same_sig(sg, h2) ? run + 1 : 0;
+      h2 = h1;
+      h1 = sg;
+      if (run >= 2 && fc < F && ((F - fc) & 1) == 0) {
+        const int R = F - fc;  // even: the book ends where it is now
+        int4* base = reinterpret_cast<int4*>(a.fills + (size_t)m * (size_t)F * 8);
+        const int4 f0a = ld_rec(base + 2 * (fc - 2)), f0b = ld_rec(base + 2 * (fc - 2) + 1);
+        const int4 f1a = ld_rec(base + 2 * (fc - 1)), f1b = ld_rec(base + 2 * (fc - 1) + 1);
+        for (int k = 0; k < R; k += 2) {
+          st_stream_v4(base + 2 * (fc + k), f0a);
+          st_stream_v4(base + 2 * (fc + k) + 1, f0b);
+          st_stream_v4(base + 2 * (fc + k + 1), f1a);
+          st_stream_v4(base + 2 * (fc + k + 1) + 1, f1b);
+        }
+        // fill record: {price, size, taker, quoter} {quote size, taker tid, quote tid, is_sell}
+        book_trade<kPos>(a, m, f0b.w ? f0a.z : f0a.w, f0b.w ? f0a.w : f0a.z, f0a.x, f0a.y, R / 2);
+        book_trade<kPos>(a, m, f1b.w ? f1a.z : f1a.w, f1b.w ? f1a.w : f1a.z, f1a.x, f1a.y, R / 2);
+        if (kEvents) {
+          e_fill += R;
+          e_rm += (R / 2) * (rm1 + rm2);
+        }
+        fc = -1;  // the next iteration finds fill_count == F (market.cu:187-195)
+        break;
+      }
       const bool bid_is_quote = B.z < A.z;  // market.cu:172
       const int price = bid_is_quote ? meta_price(B.w) : meta_price(A.w);
       const int q = min(B.x, A.x);
@@ -107,36 +217,11 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       st_stream_v4(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y));
       st_stream_v4(fr + 1, make_int4(bid_is_quote ? B.x : A.x, bid_is_quote ? A.z : B.z,
                                      bid_is_quote ? B.z : A.z, bid_is_quote ? 0 : 1));
-      // portfolios, market.cu:221-232 (buyer = bid's customer, seller = ask's).
-      // One thread owns the market, so the read-modify-writes need no
-      // atomicity; they are issued as fire-and-forget reductions (RED) so the
-      // match loop never waits for them.  int32 adds wrap like the reference's.
-      if ((uint32_t)B.y < (uint32_t)C && (uint32_t)A.y < (uint32_t)C && B.y != A.y) {
-        const int notional = wmul(price, q);
-        int* pb = a.port + ((size_t)m * C + B.y) * 2;
-        int* pa = a.port + ((size_t)m * C + A.y) * 2;
-        red_add(pb, q);
-        red_add(pb + 1, wsub(0, notional));
-        red_add(pa, wsub(0, q));
-        red_add(pa + 1, notional);
-      }  // same customer on both sides: +q-q and -n+n leave it unchanged
-      if (kPos && B.y != A.y) {
-        const long long n64 = (long long)price * (long long)q;
-        if ((uint32_t)B.y < (uint32_t)C) {
-          long long* p = a.pos + ((size_t)m * C + B.y) * 2;
-          red_add64(p, (long long)q);
-          red_add64(p + 1, -n64);
-        }
-        if ((uint32_t)A.y < (uint32_t)C) {
-          long long* p = a.pos + ((size_t)m * C + A.y) * 2;
-          red_add64(p, -(long long)q);
-          red_add64(p + 1, n64);
-        }
-      }
+      book_trade<kPos>(a, m, B.y, A.y, price, q, 1);  // buyer = bid's customer
       if (kEvents) {
         ++e_fill;
-        if ((uint32_t)B.y < 64u && B.y < C) touched |= 1ull << B.y;
-        if ((uint32_t)A.y < 64u && A.y < C) touched |= 1ull << A.y;
+        if ((uint32_t)B.y < 64u && B.y < a.C) touched |= 1ull << B.y;
+        if ((uint32_t)A.y < 64u && A.y < a.C) touched |= 1ull << A.y;
       }
       ++fc;
       // market.cu:237-238: both sizes drop by q (twice when one record heads both sides)
@@ -150,9 +235,12 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
         st_rec_size(rec + bslot, nb);
         st_rec_size(rec + aslot, na);
       }
+      B.x = nb;  // bc == bslot and ac == aslot here
+      A.x = na;
+      int rm = 0;
       if (nb == 0) {  // market.cu:241-256
         const int nx = meta_next(B.w);
-        ++e_rm;
+        ++rm;
         if (nx == -1) {
           eb = kEmptyLevel;
           lv[2 * bb] = eb;
@@ -167,7 +255,7 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       }
       if (na == 0) {  // market.cu:258-273
         const int nx = meta_next(A.w);
-        ++e_rm;
+        ++rm;
         if (nx == -1) {
           ea = kEmptyLevel;
           lv[2 * ba + 1] = ea;
@@ -180,6 +268,9 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
           lv[2 * ba + 1] = ea;
         }
       }
+      e_rm += rm;
+      rm2 = rm1;
+      rm1 = rm;
     }
     a.bk.slots[m] = ns;
     a.bk.mask[m] = bm.lo;
@@ -193,14 +284,22 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       if (bb >= 0) {
         if (eb_lvl != bb) eb = lv[2 * bb];
         const int h = lv_head(eb);
-        if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
-        else flag_state(a.bk.flag, kBadLevel);
+        if ((uint32_t)h < (uint32_t)O) {
+          obp = bb;
+          obs = h == bc ? B.x : (h == ac ? A.x : ld_rec_size(rec + h));
+        } else {
+          flag_state(a.bk.flag, kBadLevel);
+        }
       }
       if (ba < L) {
         if (ea_lvl != ba) ea = lv[2 * ba + 1];
         const int h = lv_head(ea);
-        if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
-        else flag_state(a.bk.flag, kBadLevel);
+        if ((uint32_t)h < (uint32_t)O) {
+          oap = ba;
+          oas = h == ac ? A.x : (h == bc ? B.x : ld_rec_size(rec + h));
+        } else {
+          flag_state(a.bk.flag, kBadLevel);
+        }
       }
       st_stream(a.bbp + m, obp);
       st_stream(a.bbs + m, obs);

@@ -147,3 +147,15 @@ class _SubFills:
     def __init__(self, fills, sl):
         self.fill_counts = fills.fill_counts[sl]
         self.fill_records = fills.fill_records[sl]
+
+
+@pytest.mark.parametrize("F", [5, 6, 7, 16, 33])
+def test_periodic_overflow_tails(F):
+    """Tiny rings make ring-wrap cycles (a slot heading both sides, size-0
+    self-loops) common; the fill budgets cover both parities of the fills
+    left when a period-2 loop is recognised and written in bulk."""
+    run_differential(cfg(3)["gen"], 512, 128, 4, F, 64, 300, bbo="fused", positions=True,
+                     state_every=30)
+    run_differential(cfg(4)["gen"], 512, 128, 2, F, 5, 300, bbo="fused", positions=True,
+                     state_every=30)
+    run_differential(cfg(0)["gen"], 256, 128, 1, F, 16, 200, bbo="separate", state_every=20)

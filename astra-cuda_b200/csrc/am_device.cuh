@@ -9,6 +9,10 @@
 //                                Market-minor so a warp's 32 markets read and
 //                                write each word as one coalesced 256-byte run.
 //   levels  uint32 [N][L][2]     per level and side {head:int16 | tail:int16<<16}
+//   bbo     int32  [4][N]        best-level head cache: bid head slot, its size,
+//                                ask head slot, its size, as the last step left
+//                                them; slot -1 = unknown.  Derived state: it
+//                                saves loads and makes GetBBOs coalesced.
 //   orders  int4   [N][O]        order record {size, customer id, tid,
 //                                next:int16 | price:uint8<<16 | is_bid<<24}
 //
@@ -25,7 +29,7 @@ constexpr uint32_t kEmptyLevel = 0xFFFFFFFFu;  // head = tail = -1
 constexpr int kBlock = 256;
 
 struct Layout {
-  size_t off_slots, off_mask, off_levels, off_orders, total;
+  size_t off_slots, off_mask, off_levels, off_bbo, off_orders, total;
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -36,6 +40,7 @@ __host__ __device__ inline Layout layout_of(int64_t N, int64_t L, int64_t O) {
   l.off_slots = o;  o = align256(o + 4 * (size_t)N);
   l.off_mask = o;   o = align256(o + 32 * (size_t)N);
   l.off_levels = o; o = align256(o + 8 * (size_t)N * (size_t)L);
+  l.off_bbo = o;    o = align256(o + 16 * (size_t)N);  // after the levels: both start at 0xFF
   l.off_orders = o; o = align256(o + 16 * (size_t)N * (size_t)O);
   l.total = o;
   return l;
@@ -46,6 +51,7 @@ struct BookView {
   int32_t* slots;
   unsigned long long* mask;
   uint32_t* levels;
+  int32_t* bbo;
   int4* orders;
 };
 
@@ -55,6 +61,7 @@ inline BookView view_of(void* book, int64_t N, int64_t L, int64_t O) {
   return BookView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + l.off_slots),
                   reinterpret_cast<unsigned long long*>(b + l.off_mask),
                   reinterpret_cast<uint32_t*>(b + l.off_levels),
+                  reinterpret_cast<int32_t*>(b + l.off_bbo),
                   reinterpret_cast<int4*>(b + l.off_orders)};
 }
 
@@ -94,6 +101,30 @@ __device__ __forceinline__ int mhigh(const Mask128& m) {
 // lowest occupied level, `none` if none (the best ask)
 __device__ __forceinline__ int mlow(const Mask128& m, int none) {
   return m.lo ? __ffsll((long long)m.lo) - 1 : (m.hi ? 63 + __ffsll((long long)m.hi) : none);
+}
+
+// highest occupied level strictly below p, -1 if none (p <= 127)
+__device__ __forceinline__ int mhigh_below(const Mask128& m, int p) {
+  if (p <= 0) return -1;
+  if (p <= 64) {
+    const unsigned long long lo = p == 64 ? m.lo : (m.lo & ((1ull << p) - 1));
+    return lo ? 63 - __clzll((long long)lo) : -1;
+  }
+  const unsigned long long hi = m.hi & ((1ull << (p - 64)) - 1);
+  if (hi) return 127 - __clzll((long long)hi);
+  return m.lo ? 63 - __clzll((long long)m.lo) : -1;
+}
+// lowest occupied level strictly above p, `none` if none (p >= 0)
+__device__ __forceinline__ int mlow_above(const Mask128& m, int p, int none) {
+  if (p < 63) {
+    const unsigned long long lo = m.lo & ~((2ull << p) - 1);
+    if (lo) return __ffsll((long long)lo) - 1;
+    return m.hi ? 63 + __ffsll((long long)m.hi) : none;
+  }
+  if (p == 63) return m.hi ? 63 + __ffsll((long long)m.hi) : none;
+  if (p >= 127) return none;
+  const unsigned long long hi = m.hi & ~((2ull << (p - 64)) - 1);
+  return hi ? 63 + __ffsll((long long)hi) : none;
 }
 
 // ---- memory access ----

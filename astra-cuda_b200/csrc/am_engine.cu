@@ -9,7 +9,6 @@
 #include <string>
 
 #include "am_kernels.cuh"
-#include "am_step_sm.cuh"
 #include "astra_market.h"
 
 namespace {
@@ -119,38 +118,15 @@ inline unsigned grid_stride_blocks(int64_t n) {
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-bool use_v1() {
-  static const bool v1 = [] {
-    const char* e = getenv("ASTRA_STEP_KERNEL");
-    return !(e && e[0] == '2');
+// Threads per block of the step kernel (64, 128 or 256; ASTRA_STEP_BLOCK
+// overrides the default for tuning runs).
+int step_block() {
+  static const int tpb = [] {
+    const char* e = getenv("ASTRA_STEP_BLOCK");
+    const int v = e ? atoi(e) : am::kBlock;
+    return (v == 64 || v == 128 || v == 256) ? v : am::kBlock;
   }();
-  return v1;
-}
-
-// Per device: resident warps of the state-machine step kernel, so the grid is
-// one wave of persistent warps, each owning ceil(N / warps) markets.
-template <bool kBBO, bool kPos, bool kEvents>
-int resident_warps(int device) {
-  static int cache[64] = {0};
-  if (device < 0 || device >= 64) return 148 * 32;
-  if (cache[device] == 0) {
-    int sms = 148, per_sm = 4;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, am::step_sm_kernel<kBBO, kPos, kEvents>,
-                                                  am::kBlock, 0);
-    cache[device] = sms * (per_sm > 0 ? per_sm : 1) * (am::kBlock / 32);
-  }
-  return cache[device];
-}
-
-template <bool kBBO, bool kPos, bool kEvents>
-void launch_sm(const am::StepArgs& a, int device, cudaStream_t s) {
-  const int64_t warps = resident_warps<kBBO, kPos, kEvents>(device);
-  int64_t per_warp = ((int64_t)a.N + warps - 1) / warps;
-  if (per_warp < 32) per_warp = 32;
-  const int64_t n_warps = ((int64_t)a.N + per_warp - 1) / per_warp;
-  const int64_t blocks = (n_warps * 32 + am::kBlock - 1) / am::kBlock;
-  am::step_sm_kernel<kBBO, kPos, kEvents><<<(unsigned)blocks, am::kBlock, 0, s>>>(a, (int)per_warp);
+  return tpb;
 }
 
 int check_range(const am_dims& d, int32_t market0, int32_t count) {
@@ -236,45 +212,19 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
   a.events = reinterpret_cast<unsigned long long*>(events);
   // num_markets == 0 gives an empty grid, which CUDA rejects as the
   // reference's launch does (market.cu:507-528)
-  const dim3 grid(blocks_for(d.num_markets)), block(am::kBlock);
   cudaStream_t s = as_stream(stream);
   const int variant = (n_bbo ? 1 : 0) | (positions ? 2 : 0) | (events ? 4 : 0);
-  if (use_v1()) {
-    static const int tpb = [] {
-      const char* e = getenv("ASTRA_STEP_BLOCK");
-      int v = e ? atoi(e) : am::kBlock;
-      return (v == 32 || v == 64 || v == 128 || v == 256) ? v : am::kBlock;
-    }();
-    static const bool l2_set = [] {
-      const char* e = getenv("ASTRA_L2_FETCH");
-      if (e) cudaDeviceSetLimit(cudaLimitMaxL2FetchGranularity, (size_t)atoi(e));
-      return true;
-    }();
-    (void)l2_set;
-    const dim3 grid2(blocks_for(d.num_markets) * (am::kBlock / tpb)), block2(tpb);
-    const dim3& grid = grid2;
-    const dim3& block = block2;
-    switch (variant) {
-      case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
-      case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
-      case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
-      case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
-      case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
-      case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
-      case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
-      default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
-    }
-    return launch_status("AddTwoSidedQuotes");
-  }
+  const int tpb = step_block();
+  const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
   switch (variant) {
-    case 0: launch_sm<false, false, false>(a, mk->device, s); break;
-    case 1: launch_sm<true, false, false>(a, mk->device, s); break;
-    case 2: launch_sm<false, true, false>(a, mk->device, s); break;
-    case 3: launch_sm<true, true, false>(a, mk->device, s); break;
-    case 4: launch_sm<false, false, true>(a, mk->device, s); break;
-    case 5: launch_sm<true, false, true>(a, mk->device, s); break;
-    case 6: launch_sm<false, true, true>(a, mk->device, s); break;
-    default: launch_sm<true, true, true>(a, mk->device, s); break;
+    case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
+    case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
+    case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
+    case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
+    case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
+    case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
+    case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
+    default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
   }
   return launch_status("AddTwoSidedQuotes");
 }

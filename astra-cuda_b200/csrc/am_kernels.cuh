@@ -27,41 +27,74 @@ struct StepArgs {
   unsigned long long* events;  // [5] or null
 };
 
+// Records whose contents the thread knows without a load: two full head
+// records (B in slot bc, A in slot ac) and the two head sizes the previous
+// step left in the BBO cache (slot cbh -> cbs, cah -> cas).  Every record
+// write the thread makes is reported through note_* so all four stay equal
+// to memory; slot -1 means "none" and never matches.
+struct Known {
+  int4 B, A;
+  int bc, ac;
+  int cbh, cbs, cah, cas;
+};
+__device__ __forceinline__ void note_record(Known& k, int slot, const int4& v) {
+  if (k.bc == slot) k.B = v;
+  if (k.ac == slot) k.A = v;
+  if (k.cbh == slot) k.cbs = v.x;
+  if (k.cah == slot) k.cas = v.x;
+}
+__device__ __forceinline__ void note_size(Known& k, int slot, int sz) {
+  if (k.bc == slot) k.B.x = sz;
+  if (k.ac == slot) k.A.x = sz;
+  if (k.cbh == slot) k.cbs = sz;
+  if (k.cah == slot) k.cas = sz;
+}
+__device__ __forceinline__ void note_next(Known& k, int slot, int nx) {
+  if (k.bc == slot) k.B.w = make_meta(nx, meta_price(k.B.w), meta_is_bid(k.B.w));
+  if (k.ac == slot) k.A.w = make_meta(nx, meta_price(k.A.w), meta_is_bid(k.A.w));
+}
+__device__ __forceinline__ bool known_size(const Known& k, int slot, int& sz) {
+  if (slot == k.bc) { sz = k.B.x; return true; }
+  if (slot == k.ac) { sz = k.A.x; return true; }
+  if (slot == k.cbh) { sz = k.cbs; return true; }
+  if (slot == k.cah) { sz = k.cas; return true; }
+  return false;
+}
+
 // Adds one order to side `side` (0 bid, 1 ask) at level `px`; `e` is that
 // level's entry, loaded by the caller.  Restates add_orders_kernel
 // (market.cu:45-69 / :74-98): take slot = counter++ % O, write the record
-// with no successor, append it to the level's FIFO.  Keeps the two cached
-// records (slot bc -> B, slot ac -> A) equal to memory; returns the new
-// record's slot when it became the level's head (its record is then known
-// without a load), else -1.
+// with no successor, append it to the level's FIFO.  Returns the slot
+// written; `became_head` tells whether the order is now the level's head and
+// `linked` which record got the new successor link (-1: none).
 __device__ __forceinline__ int insert_order(const StepArgs& a, int4* rec, uint32_t* lv, int side,
                                             int px, int sz, int cid, int tid, int& ns,
-                                            uint32_t& e, Mask128& mask, int4& B, int& bc,
-                                            int4& A, int& ac, int4& v) {
+                                            uint32_t& e, Mask128& mask, Known& k, int4& v,
+                                            bool& became_head, int& linked) {
   const int slot = (int)((uint32_t)ns % (uint32_t)a.O);
   ns = wadd(ns, 1);
   v = make_int4(sz, cid, tid, make_meta(-1, px, side == 0 ? 1 : 0));
   st_rec(rec + slot, v);
-  if (bc == slot) B = v;
-  if (ac == slot) A = v;
-  int head_slot = -1;
+  note_record(k, slot, v);
+  linked = -1;
   const int old_tail = lv_tail(e);
   if (old_tail == -1) {
     e = lv_make(slot, slot);
     mset(mask, px);
-    head_slot = slot;
+    became_head = true;
   } else {
     e = lv_make(lv_head(e), slot);
+    became_head = false;
     if ((uint32_t)old_tail < (uint32_t)a.O) {
       st_rec_next(rec + old_tail, slot);
-      if (bc == old_tail) B.w = make_meta(slot, meta_price(B.w), meta_is_bid(B.w));
-      if (ac == old_tail) A.w = make_meta(slot, meta_price(A.w), meta_is_bid(A.w));
+      note_next(k, old_tail, slot);
+      linked = old_tail;
     } else {
       flag_state(a.bk.flag, kBadSlot);
     }
   }
   lv[2 * px + side] = e;
-  return head_slot;
+  return slot;
 }
 
 // Portfolio and int64-position updates of `reps` identical fills
@@ -123,62 +156,111 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
   if (m < a.N) {
     const size_t N = (size_t)a.N;
     const int L = a.L, O = a.O, F = a.F;
+    // ---- round 1: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
     const int bp = ld_stream(a.bid_px + m), bs = ld_stream(a.bid_sz + m);
     const int ap = ld_stream(a.ask_px + m), as = ld_stream(a.ask_sz + m);
     const int cid = ld_stream(a.cids + m);
     int ns = a.bk.slots[m];
     Mask128 bm{a.bk.mask[m], a.bk.mask[N + m]};
     Mask128 am_{a.bk.mask[2 * N + m], a.bk.mask[3 * N + m]};
+    Known k;
+    k.bc = -1;
+    k.ac = -1;
+    k.cbh = a.bk.bbo[m];
+    k.cbs = a.bk.bbo[N + m];
+    k.cah = a.bk.bbo[2 * N + m];
+    k.cas = a.bk.bbo[3 * N + m];
     uint32_t* lv = a.bk.levels + (size_t)m * (size_t)L * 2;
     int4* rec = a.bk.orders + (size_t)m * (size_t)O;
 
     // market.cu:44 / :73 -- a negative price is undefined there; not added here
     const bool add_b = bs > 0 && bp < L && bp >= 0;
     const bool add_a = as > 0 && ap < L && ap >= 0;
-    // both level entries are independent: issue the loads together
-    uint32_t eb = add_b ? lv[2 * bp] : kEmptyLevel;
-    uint32_t ea = add_a ? lv[2 * ap + 1] : kEmptyLevel;
-    int eb_lvl = -2, ea_lvl = -2;  // level whose entry eb / ea holds
-    int4 B = make_int4(0, 0, 0, 0), A = B, v;
-    int bc = -1, ac = -1;           // slots whose records B / A hold (-1: none)
+    const int ob = mhigh(bm), oa = mlow(am_, L);  // best levels before inserting
+
+    // ---- round 2: everything the inserts and the first match need ----
+    // After inserting, the best bid is max(ob, bp) and the best ask min(oa, ap),
+    // so these four entries cover both; the cached head record of the best
+    // level a new quote crosses is fetched at the same time.
+    uint32_t eb_ins = add_b ? lv[2 * bp] : kEmptyLevel;
+    uint32_t ea_ins = add_a ? lv[2 * ap + 1] : kEmptyLevel;
+    const uint32_t eb_old = (ob >= 0 && !(add_b && ob == bp)) ? lv[2 * ob] : kEmptyLevel;
+    const uint32_t ea_old = (oa < L && !(add_a && oa == ap)) ? lv[2 * oa + 1] : kEmptyLevel;
+    int4 PB = make_int4(0, 0, 0, 0), PA = PB;  // speculative head records ...
+    int pb = -1, pa = -1;                      // ... of these slots (-1: none)
+    if (add_a && ob >= 0 && ap <= ob && (uint32_t)k.cbh < (uint32_t)O) {
+      PB = ld_rec(rec + k.cbh);
+      pb = k.cbh;
+    }
+    if (add_b && oa < L && bp >= oa && (uint32_t)k.cah < (uint32_t)O) {
+      PA = ld_rec(rec + k.cah);
+      pa = k.cah;
+    }
+
+    int4 v;
+    bool head;
+    int linked;
     if (add_b) {
-      const int h = insert_order(a, rec, lv, 0, bp, bs, cid, a.base_tid, ns, eb, bm, B, bc, A, ac, v);
-      if (h >= 0) { B = v; bc = h; }
-      eb_lvl = bp;
+      const int sl = insert_order(a, rec, lv, 0, bp, bs, cid, a.base_tid, ns, eb_ins, bm, k, v,
+                                  head, linked);
+      if (head) { k.B = v; k.bc = sl; }
+      if (sl == pb || linked == pb) pb = -1;  // the prefetched record changed
+      if (sl == pa || linked == pa) pa = -1;
       ++e_ins;
     }
     if (add_a) {
-      const int h = insert_order(a, rec, lv, 1, ap, as, cid, wadd(a.base_tid, 1), ns, ea, am_,
-                                 B, bc, A, ac, v);
-      if (h >= 0) { A = v; ac = h; }
-      ea_lvl = ap;
+      const int sl = insert_order(a, rec, lv, 1, ap, as, cid, wadd(a.base_tid, 1), ns, ea_ins,
+                                  am_, k, v, head, linked);
+      if (head) { k.A = v; k.ac = sl; }
+      if (sl == pb || linked == pb) pb = -1;
+      if (sl == pa || linked == pa) pa = -1;
       ++e_ins;
     }
 
     // match_orders_kernel, market.cu:120-274
     int bb = mhigh(bm), ba = mlow(am_, L);
+    uint32_t eb = (add_b && bb == bp) ? eb_ins : eb_old;
+    uint32_t ea = (add_a && ba == ap) ? ea_ins : ea_old;
+    int eb_lvl = bb, ea_lvl = ba;  // level whose entry eb / ea holds (-2: none)
+    uint32_t eb2 = kEmptyLevel, ea2 = kEmptyLevel;  // next-best entries, prefetched
+    int eb2_lvl = -2, ea2_lvl = -2;
     int fc = 0;
     Sig h1{~0ull, 0}, h2{~0ull, 0};  // signatures of the previous two iterations
     int run = 0;                     // consecutive iterations equal to the one two before
     int rm1 = 0, rm2 = 0;            // removals made by those two iterations
     while (bb >= 0 && ba < L && bb >= ba) {
-      if (eb_lvl != bb) { eb = lv[2 * bb]; eb_lvl = bb; }
-      if (ea_lvl != ba) { ea = lv[2 * ba + 1]; ea_lvl = ba; }
+      if (eb_lvl != bb) { eb = (bb == eb2_lvl) ? eb2 : lv[2 * bb]; eb_lvl = bb; }
+      if (ea_lvl != ba) { ea = (ba == ea2_lvl) ? ea2 : lv[2 * ba + 1]; ea_lvl = ba; }
       const int bslot = lv_head(eb), aslot = lv_head(ea);
       if (bslot == -1 || aslot == -1) break;  // market.cu:155
       if ((uint32_t)bslot >= (uint32_t)O || (uint32_t)aslot >= (uint32_t)O) {
         flag_state(a.bk.flag, kBadSlot);
         break;
       }
-      // head records: reuse the cached copy of a slot, load only a new head
-      if (bc != bslot) {
-        if (ac == bslot) B = A; else B = ld_rec(rec + bslot);
-        bc = bslot;
+      // next-best levels: needed only if a best level empties; fetched now so
+      // that costs no extra round trip (the bits below bb / above ba do not
+      // change while matching)
+      const int nb2 = mhigh_below(bm, bb), na2 = mlow_above(am_, ba, L);
+      if (nb2 >= 0 && nb2 != eb2_lvl) { eb2 = lv[2 * nb2]; eb2_lvl = nb2; }
+      if (na2 < L && na2 != ea2_lvl) { ea2 = lv[2 * na2 + 1]; ea2_lvl = na2; }
+      // head records: a known copy, the prefetch, or a load
+      if (k.bc != bslot) {
+        if (k.ac == bslot) k.B = k.A;
+        else if (pb == bslot) k.B = PB;
+        else if (pa == bslot) k.B = PA;
+        else k.B = ld_rec(rec + bslot);
+        k.bc = bslot;
       }
-      if (ac != aslot) {
-        if (bc == aslot) A = B; else A = ld_rec(rec + aslot);
-        ac = aslot;
+      if (k.ac != aslot) {
+        if (k.bc == aslot) k.A = k.B;
+        else if (pa == aslot) k.A = PA;
+        else if (pb == aslot) k.A = PB;
+        else k.A = ld_rec(rec + aslot);
+        k.ac = aslot;
       }
+      pb = -1;  // prefetches serve the first iteration only
+      pa = -1;
+      const int4 B = k.B, A = k.A;
       // A run of two iterations that each repeat the one two before makes
       // the loop periodic with period 2 from there on (period 1 included):
       // every later iteration reads exactly what the one two before read.
@@ -192,11 +274,11 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
         int4* base = reinterpret_cast<int4*>(a.fills + (size_t)m * (size_t)F * 8);
         const int4 f0a = ld_rec(base + 2 * (fc - 2)), f0b = ld_rec(base + 2 * (fc - 2) + 1);
         const int4 f1a = ld_rec(base + 2 * (fc - 1)), f1b = ld_rec(base + 2 * (fc - 1) + 1);
-        for (int k = 0; k < R; k += 2) {
-          st_stream_v4(base + 2 * (fc + k), f0a);
-          st_stream_v4(base + 2 * (fc + k) + 1, f0b);
-          st_stream_v4(base + 2 * (fc + k + 1), f1a);
-          st_stream_v4(base + 2 * (fc + k + 1) + 1, f1b);
+        for (int j = 0; j < R; j += 2) {
+          st_stream_v4(base + 2 * (fc + j), f0a);
+          st_stream_v4(base + 2 * (fc + j) + 1, f0b);
+          st_stream_v4(base + 2 * (fc + j + 1), f1a);
+          st_stream_v4(base + 2 * (fc + j + 1) + 1, f1b);
         }
         // fill record: {price, size, taker, quoter} {quote size, taker tid, quote tid, is_sell}
         book_trade<kPos>(a, m, f0b.w ? f0a.z : f0a.w, f0b.w ? f0a.w : f0a.z, f0a.x, f0a.y, R / 2);
@@ -229,14 +311,15 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       if (bslot == aslot) {
         nb = na = wsub(wsub(B.x, q), q);
         st_rec_size(rec + bslot, nb);
+        note_size(k, bslot, nb);
       } else {
         nb = wsub(B.x, q);
         na = wsub(A.x, q);
         st_rec_size(rec + bslot, nb);
         st_rec_size(rec + aslot, na);
+        note_size(k, bslot, nb);
+        note_size(k, aslot, na);
       }
-      B.x = nb;  // bc == bslot and ac == aslot here
-      A.x = na;
       int rm = 0;
       if (nb == 0) {  // market.cu:241-256
         const int nx = meta_next(B.w);
@@ -279,32 +362,41 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
     a.bk.mask[3 * N + m] = am_.hi;
     st_stream(a.fill_counts + m, fc);  // market.cu:277 (or -1 from :193)
 
-    if (kBBO) {  // get_bbo_kernel on the post-match book, market.cu:291-319
-      int obp = -1, obs = 0, oap = -1, oas = 0;
-      if (bb >= 0) {
-        if (eb_lvl != bb) eb = lv[2 * bb];
-        const int h = lv_head(eb);
-        if ((uint32_t)h < (uint32_t)O) {
-          obp = bb;
-          obs = h == bc ? B.x : (h == ac ? A.x : ld_rec_size(rec + h));
-        } else {
-          flag_state(a.bk.flag, kBadLevel);
-        }
+    // get_bbo_kernel on the post-match book (market.cu:291-319): the head
+    // sizes come from known records when possible; the result also refreshes
+    // the BBO cache (a size that would need a load is left unknown when no BBO
+    // output is asked for).
+    int b_slot = -1, b_sz = 0, a_slot = -1, a_sz = 0;
+    if (bb >= 0) {
+      if (eb_lvl != bb) eb = (bb == eb2_lvl) ? eb2 : lv[2 * bb];
+      const int h = lv_head(eb);
+      if ((uint32_t)h < (uint32_t)O) {
+        if (known_size(k, h, b_sz)) b_slot = h;
+        else if (kBBO) { b_sz = ld_rec_size(rec + h); b_slot = h; }
+      } else {
+        flag_state(a.bk.flag, kBadLevel);
       }
-      if (ba < L) {
-        if (ea_lvl != ba) ea = lv[2 * ba + 1];
-        const int h = lv_head(ea);
-        if ((uint32_t)h < (uint32_t)O) {
-          oap = ba;
-          oas = h == ac ? A.x : (h == bc ? B.x : ld_rec_size(rec + h));
-        } else {
-          flag_state(a.bk.flag, kBadLevel);
-        }
+    }
+    if (ba < L) {
+      if (ea_lvl != ba) ea = (ba == ea2_lvl) ? ea2 : lv[2 * ba + 1];
+      const int h = lv_head(ea);
+      if ((uint32_t)h < (uint32_t)O) {
+        if (known_size(k, h, a_sz)) a_slot = h;
+        else if (kBBO) { a_sz = ld_rec_size(rec + h); a_slot = h; }
+      } else {
+        flag_state(a.bk.flag, kBadLevel);
       }
-      st_stream(a.bbp + m, obp);
-      st_stream(a.bbs + m, obs);
-      st_stream(a.bap + m, oap);
-      st_stream(a.bas + m, oas);
+    }
+    a.bk.bbo[m] = b_slot;
+    a.bk.bbo[N + m] = b_sz;
+    a.bk.bbo[2 * N + m] = a_slot;
+    a.bk.bbo[3 * N + m] = a_sz;
+    if (kBBO) {
+      const bool hb = bb >= 0 && b_slot >= 0, ha = ba < L && a_slot >= 0;
+      st_stream(a.bbp + m, hb ? bb : -1);
+      st_stream(a.bbs + m, hb ? b_sz : 0);
+      st_stream(a.bap + m, ha ? ba : -1);
+      st_stream(a.bas + m, ha ? a_sz : 0);
     }
   }
   if (kEvents) {
@@ -327,7 +419,9 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
   }
 }
 
-// get_bbo_kernel (market.cu:280-320) from the occupancy masks.
+// get_bbo_kernel (market.cu:280-320) from the occupancy masks and the BBO
+// cache the last step left; only a side whose cached head is unknown reads
+// its level entry and head record.
 __global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, int O,
                                                      int32_t* bbp, int32_t* bbs, int32_t* bap,
                                                      int32_t* bas) {
@@ -336,20 +430,25 @@ __global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, 
   const size_t n = (size_t)N;
   const Mask128 bm{bk.mask[m], bk.mask[n + m]}, am_{bk.mask[2 * n + m], bk.mask[3 * n + m]};
   const int bb = mhigh(bm), ba = mlow(am_, L);
+  const int cb = bk.bbo[m], cbs = bk.bbo[n + m], ca = bk.bbo[2 * n + m], cas = bk.bbo[3 * n + m];
   const uint32_t* lv = bk.levels + (size_t)m * (size_t)L * 2;
   const int4* rec = bk.orders + (size_t)m * (size_t)O;
-  const uint32_t eb = bb >= 0 ? lv[2 * bb] : kEmptyLevel;
-  const uint32_t ea = ba < L ? lv[2 * ba + 1] : kEmptyLevel;
   int obp = -1, obs = 0, oap = -1, oas = 0;
   if (bb >= 0) {
-    const int h = lv_head(eb);
-    if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
-    else flag_state(bk.flag, kBadLevel);
+    if (cb >= 0) { obp = bb; obs = cbs; }
+    else {
+      const int h = lv_head(lv[2 * bb]);
+      if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
+      else flag_state(bk.flag, kBadLevel);
+    }
   }
   if (ba < L) {
-    const int h = lv_head(ea);
-    if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
-    else flag_state(bk.flag, kBadLevel);
+    if (ca >= 0) { oap = ba; oas = cas; }
+    else {
+      const int h = lv_head(lv[2 * ba + 1]);
+      if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
+      else flag_state(bk.flag, kBadLevel);
+    }
   }
   st_stream(bbp + m, obp);
   st_stream(bbs + m, obs);
@@ -393,6 +492,8 @@ __global__ void clear_levels_kernel(BookView bk, int N, int L, const uint8_t* ma
     if (!mask[m]) continue;
     bk.slots[m] = 0;
     for (int w = 0; w < 4; ++w) bk.mask[w * (size_t)N + m] = 0ull;
+    bk.bbo[m] = -1;                  // BBO cache: unknown
+    bk.bbo[2 * (size_t)N + m] = -1;
   }
 }
 
@@ -463,6 +564,8 @@ __global__ void import_kernel(BookView bk, int N, int m0, int count, int L, int 
     }
     bk.mask[m] = bm.lo; bk.mask[(size_t)N + m] = bm.hi;
     bk.mask[2 * (size_t)N + m] = am_.lo; bk.mask[3 * (size_t)N + m] = am_.hi;
+    bk.bbo[m] = -1;                  // BBO cache: unknown
+    bk.bbo[2 * (size_t)N + m] = -1;
   }
 }
 

@@ -129,6 +129,16 @@ int step_block() {
   return tpb;
 }
 
+// Register cap of the step kernel for tuning runs: ASTRA_STEP_MINB = 4 asks for
+// four resident 256-thread blocks per SM (64 registers per thread).
+int step_min_blocks() {
+  static const int v = [] {
+    const char* e = getenv("ASTRA_STEP_MINB");
+    return e ? atoi(e) : 3;
+  }();
+  return v;
+}
+
 int check_range(const am_dims& d, int32_t market0, int32_t count) {
   if (market0 < 0 || count < 0 || (int64_t)market0 + count > d.num_markets)
     return fail(AM_ERR_INVALID, "market range [%d, %d) outside [0, %d)", market0,
@@ -216,6 +226,10 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
   const int variant = (n_bbo ? 1 : 0) | (positions ? 2 : 0) | (events ? 4 : 0);
   const int tpb = step_block();
   const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
+  if (variant == 3 && step_min_blocks() == 4) {
+    am::step_kernel<true, true, false, 4><<<grid, block, 0, s>>>(a);
+    return launch_status("AddTwoSidedQuotes");
+  }
   switch (variant) {
     case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
     case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;

@@ -138,6 +138,7 @@ __device__ __forceinline__ void book_trade(const StepArgs& a, int m, int buyer, 
 struct Sig {
   unsigned long long k, s;
 };
+constexpr int kTrackFrom = 4;  // fills written before loop signatures are kept
 __device__ __forceinline__ Sig make_sig(int bb, int ba, int bslot, int aslot, int bsz, int asz) {
   return Sig{(unsigned long long)(uint32_t)bb | ((unsigned long long)(uint32_t)ba << 8) |
                  ((unsigned long long)(uint32_t)bslot << 16) |
@@ -148,8 +149,8 @@ __device__ __forceinline__ bool same_sig(const Sig& x, const Sig& y) {
   return x.k == y.k && x.s == y.s;
 }
 
-template <bool kBBO, bool kPos, bool kEvents>
-__global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
+template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3>
+__global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs a) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   int e_ins = 0, e_fill = 0, e_rm = 0, e_empty = 0;
   unsigned long long touched = 0;
@@ -222,8 +223,9 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
     uint32_t eb = (add_b && bb == bp) ? eb_ins : eb_old;
     uint32_t ea = (add_a && ba == ap) ? ea_ins : ea_old;
     int eb_lvl = bb, ea_lvl = ba;  // level whose entry eb / ea holds (-2: none)
-    uint32_t eb2 = kEmptyLevel, ea2 = kEmptyLevel;  // next-best entries, prefetched
-    int eb2_lvl = -2, ea2_lvl = -2;
+    uint32_t eb2 = kEmptyLevel, ea2 = kEmptyLevel;  // next-best entries, prefetched ...
+    int eb2_lvl = -2, ea2_lvl = -2;                  // ... of these levels
+    int eb2_for = -2, ea2_for = -2;                  // best levels they were fetched for
     int fc = 0;
     Sig h1{~0ull, 0}, h2{~0ull, 0};  // signatures of the previous two iterations
     int run = 0;                     // consecutive iterations equal to the one two before
@@ -237,12 +239,19 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
         flag_state(a.bk.flag, kBadSlot);
         break;
       }
-      // next-best levels: needed only if a best level empties; fetched now so
-      // that costs no extra round trip (the bits below bb / above ba do not
-      // change while matching)
-      const int nb2 = mhigh_below(bm, bb), na2 = mlow_above(am_, ba, L);
-      if (nb2 >= 0 && nb2 != eb2_lvl) { eb2 = lv[2 * nb2]; eb2_lvl = nb2; }
-      if (na2 < L && na2 != ea2_lvl) { ea2 = lv[2 * na2 + 1]; ea2_lvl = na2; }
+      // next-best levels: needed only if a best level empties; fetched when a
+      // best level changes so an emptied level costs no extra round trip (the
+      // bits below bb / above ba do not change while matching)
+      if (bb != eb2_for) {
+        const int nb2 = mhigh_below(bm, bb);
+        if (nb2 >= 0 && nb2 != eb2_lvl) { eb2 = lv[2 * nb2]; eb2_lvl = nb2; }
+        eb2_for = bb;
+      }
+      if (ba != ea2_for) {
+        const int na2 = mlow_above(am_, ba, L);
+        if (na2 < L && na2 != ea2_lvl) { ea2 = lv[2 * na2 + 1]; ea2_lvl = na2; }
+        ea2_for = ba;
+      }
       // head records: a known copy, the prefetch, or a load
       if (k.bc != bslot) {
         if (k.ac == bslot) k.B = k.A;
@@ -265,10 +274,14 @@ __global__ void __launch_bounds__(kBlock) step_kernel(const StepArgs a) {
       // the loop periodic with period 2 from there on (period 1 included):
       // every later iteration reads exactly what the one two before read.
       // The remaining fills then repeat the last two; write them in bulk.
-      const Sig sg = make_sig(bb, ba, bslot, aslot, B.x, A.x);
-      run = same_sig(sg, h2) ? run + 1 : 0;
-      h2 = h1;
-      h1 = sg;
+      // Tracking starts at the fifth fill: shorter loops never repeat long
+      // enough to matter, and they are almost all of them.
+      if (fc >= kTrackFrom) {
+        const Sig sg = make_sig(bb, ba, bslot, aslot, B.x, A.x);
+        run = same_sig(sg, h2) ? run + 1 : 0;
+        h2 = h1;
+        h1 = sg;
+      }
       if (run >= 2 && fc < F && ((F - fc) & 1) == 0) {
         const int R = F - fc;  // even: the book ends where it is now
         int4* base = reinterpret_cast<int4*>(a.fills + (size_t)m * (size_t)F * 8);

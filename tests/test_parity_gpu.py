@@ -149,7 +149,7 @@ class _SubFills:
         self.fill_records = fills.fill_records[sl]
 
 
-@pytest.mark.parametrize("F", [5, 6, 7, 16, 33])
+@pytest.mark.parametrize("F", [5, 9, 10, 11, 16, 33])
 def test_periodic_overflow_tails(F):
     """Tiny rings make ring-wrap cycles (a slot heading both sides, size-0
     self-loops) common; the fill budgets cover both parities of the fills

@@ -18,6 +18,16 @@
 //
 // Every access a step makes to a level or an order is a single 4- or 16-byte
 // access inside one 32-byte sector, so each costs one sector of DRAM traffic.
+//
+// The masks are the authority on which levels are live.  In every state the
+// reference can reach, a level's head is -1 exactly when its tail is, and a
+// record at or past the slot counter (while the counter is below O) was not
+// written since the last Reset/ClearQuotes, so its `next` is -1.  The book
+// therefore stores neither fact: a level whose bit is clear reads as
+// head = tail = -1 whatever its entry holds (a step never loads it, and does
+// not rewrite the entry of a level it empties), and the export reports
+// next = -1 for records past the counter.  Reset and ClearQuotes touch only
+// the per-market words (counter, masks, BBO cache), and portfolios for Reset.
 #pragma once
 
 #include <cstddef>
@@ -93,6 +103,9 @@ __device__ __forceinline__ void mset(Mask128& m, int p) {
 }
 __device__ __forceinline__ void mclr(Mask128& m, int p) {
   if (p < 64) m.lo &= ~(1ull << p); else m.hi &= ~(1ull << (p - 64));
+}
+__device__ __forceinline__ bool mtest(const Mask128& m, int p) {
+  return ((p < 64 ? m.lo >> p : m.hi >> (p - 64)) & 1ull) != 0;
 }
 // highest occupied level, -1 if none (the best bid)
 __device__ __forceinline__ int mhigh(const Mask128& m) {

@@ -184,9 +184,7 @@ int am_book_init(const am_market* mk, void* stream) {
   if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in book init: %s", cudaGetErrorString(e));
   const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
   if (total > 0)
-    am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(view(mk), total,
-                                                                       d.max_active_orders_per_market,
-                                                                       false, nullptr);
+    am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(view(mk), total);
   return launch_status("VecMarket constructor");
 }
 
@@ -281,16 +279,15 @@ int am_reset(const am_market* mk, void* stream) {
   const am::Layout l = am::layout_of(d.num_markets, d.max_price_levels, d.max_active_orders_per_market);
   char* b = static_cast<char*>(mk->book);
   cudaStream_t s = as_stream(stream);
-  // slots + masks = 0, levels = -1 (market.cu:699-709); the flag is kept
+  // market.cu:693-716: slot counters and masks 0 (every level empty), BBO
+  // cache unknown, portfolios 0; the flag is kept.  Level entries and record
+  // links are not rewritten: a clear mask bit reads as an empty level and a
+  // record past the counter as next = -1.
   cudaError_t e = cudaMemsetAsync(b + l.off_slots, 0, l.off_levels - l.off_slots, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_levels, 0xFF, l.off_orders - l.off_levels, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_bbo, 0xFF, l.off_orders - l.off_bbo, s);
   if (e == cudaSuccess && d.num_customers > 0 && d.num_markets > 0)
     e = cudaMemsetAsync(mk->portfolios, 0, (size_t)d.num_markets * d.num_customers * 8, s);
   if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in Reset: %s", cudaGetErrorString(e));
-  const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
-  if (total > 0)
-    am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(
-        view(mk), total, d.max_active_orders_per_market, true, nullptr);
   return launch_status("Reset");
 }
 
@@ -302,15 +299,8 @@ int am_clear_quotes(const am_market* mk, const uint8_t* mask, void* stream) {
   if (!mask) return fail(AM_ERR_INVALID, "reset_indices is NULL");
   DeviceGuard g(mk->device);
   if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
-  cudaStream_t s = as_stream(stream);
-  const int64_t total = (int64_t)d.num_markets * d.max_active_orders_per_market;
-  am::records_kernel<<<grid_stride_blocks(total), am::kBlock, 0, s>>>(
-      view(mk), total, d.max_active_orders_per_market, true, mask);
-  int rc2 = launch_status("ClearQuotes");
-  if (rc2) return rc2;
-  const int64_t lv = (int64_t)d.num_markets * d.max_price_levels * 2;
-  am::clear_levels_kernel<<<grid_stride_blocks(lv > d.num_markets ? lv : d.num_markets), am::kBlock, 0, s>>>(
-      view(mk), d.num_markets, d.max_price_levels, mask);
+  am::clear_markets_kernel<<<blocks_for(d.num_markets), am::kBlock, 0, as_stream(stream)>>>(
+      view(mk), d.num_markets, mask);
   return launch_status("ClearQuotes");
 }
 
@@ -335,7 +325,8 @@ int am_export_state(const am_market* mk, int32_t market0, int32_t count, int32_t
                                           ? d.max_active_orders_per_market
                                           : d.max_price_levels);
   am::export_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(
-      view(mk), market0, count, d.max_price_levels, d.max_active_orders_per_market, r);
+      view(mk), d.num_markets, market0, count, d.max_price_levels,
+      d.max_active_orders_per_market, r);
   return launch_status("export_state");
 }
 

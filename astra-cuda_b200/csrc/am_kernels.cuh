@@ -183,8 +183,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     // After inserting, the best bid is max(ob, bp) and the best ask min(oa, ap),
     // so these four entries cover both; the cached head record of the best
     // level a new quote crosses is fetched at the same time.
-    uint32_t eb_ins = add_b ? lv[2 * bp] : kEmptyLevel;
-    uint32_t ea_ins = add_a ? lv[2 * ap + 1] : kEmptyLevel;
+    uint32_t eb_ins = (add_b && mtest(bm, bp)) ? lv[2 * bp] : kEmptyLevel;
+    uint32_t ea_ins = (add_a && mtest(am_, ap)) ? lv[2 * ap + 1] : kEmptyLevel;
     const uint32_t eb_old = (ob >= 0 && !(add_b && ob == bp)) ? lv[2 * ob] : kEmptyLevel;
     const uint32_t ea_old = (oa < L && !(add_a && oa == ap)) ? lv[2 * oa + 1] : kEmptyLevel;
     int4 PB = make_int4(0, 0, 0, 0), PA = PB;  // speculative head records ...
@@ -337,9 +337,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       if (nb == 0) {  // market.cu:241-256
         const int nx = meta_next(B.w);
         ++rm;
-        if (nx == -1) {
+        if (nx == -1) {  // head = tail = -1: the cleared bit says it
           eb = kEmptyLevel;
-          lv[2 * bb] = eb;
           mclr(bm, bb);
           bb = mhigh(bm);
           eb_lvl = -2;
@@ -354,7 +353,6 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
         ++rm;
         if (nx == -1) {
           ea = kEmptyLevel;
-          lv[2 * ba + 1] = ea;
           mclr(am_, ba);
           ba = mlow(am_, L);
           ea_lvl = -2;
@@ -479,35 +477,25 @@ __global__ void __launch_bounds__(kBlock) last_price_kernel(int N, int F, int32_
   if (c > 0 && c <= F) last[m] = fills[((size_t)m * (size_t)F + (size_t)(c - 1)) * 8];
 }
 
-// Constructor / Reset state of the order records: a record is zero except
-// its link (-1) -- market.cu:368-373.  With keep_fields, only the link is
-// cleared (Reset, market.cu:706, and ClearQuotes, :744-745, for masked markets).
-__global__ void records_kernel(BookView bk, int64_t total, int O, bool keep_fields,
-                               const uint8_t* mask) {
+// Constructor state of the order records: a record is zero except its link
+// (-1) -- market.cu:368-373.
+__global__ void records_kernel(BookView bk, int64_t total) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    if (mask && !mask[i / O]) continue;
-    if (keep_fields) st_rec_next(bk.orders + i, -1);
-    else st_rec(bk.orders + i, make_int4(0, 0, 0, make_meta(-1, 0, 0)));
-  }
+       i += (int64_t)gridDim.x * blockDim.x)
+    st_rec(bk.orders + i, make_int4(0, 0, 0, make_meta(-1, 0, 0)));
 }
 
-// ClearQuotes for levels, slot counters and masks of masked markets.
-__global__ void clear_levels_kernel(BookView bk, int N, int L, const uint8_t* mask) {
-  const int64_t total = (int64_t)N * L * 2;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / (2 * (int64_t)L);
-    if (mask[m]) bk.levels[i] = kEmptyLevel;
-  }
-  for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < N;
-       m += (int64_t)gridDim.x * blockDim.x) {
-    if (!mask[m]) continue;
-    bk.slots[m] = 0;
-    for (int w = 0; w < 4; ++w) bk.mask[w * (size_t)N + m] = 0ull;
-    bk.bbo[m] = -1;                  // BBO cache: unknown
-    bk.bbo[2 * (size_t)N + m] = -1;
-  }
+// ClearQuotes (market.cu:718-756) for the masked markets: slot counter 0,
+// every level empty (its mask bits cleared), BBO cache unknown.  The level
+// entries and record links the reference rewrites are not touched: a clear
+// bit reads as an empty level and a record past the counter as next = -1.
+__global__ void clear_markets_kernel(BookView bk, int N, const uint8_t* mask) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= N || !mask[m]) return;
+  bk.slots[m] = 0;
+  for (int w = 0; w < 4; ++w) bk.mask[w * (size_t)N + m] = 0ull;
+  bk.bbo[m] = -1;
+  bk.bbo[2 * (size_t)N + m] = -1;
 }
 
 struct RefState {
@@ -518,8 +506,11 @@ struct RefState {
 };
 
 // Book -> reference layout for markets [m0, m0+count); outputs are indexed
-// from market m0.
-__global__ void export_kernel(BookView bk, int m0, int count, int L, int O, RefState r) {
+// from market m0.  N is the book's market count (the mask stride).  A level
+// whose mask bit is clear is reported empty, and a record at or past the slot
+// counter (while the counter is below O) with next = -1: the values the
+// reference's Reset / ClearQuotes write (market.cu:699-706, :739-745).
+__global__ void export_kernel(BookView bk, int N, int m0, int count, int L, int O, RefState r) {
   const int64_t n_rec = (int64_t)count * O, n_lv = (int64_t)count * L;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -527,12 +518,19 @@ __global__ void export_kernel(BookView bk, int m0, int count, int L, int O, RefS
   const uint32_t* levels = bk.levels + (size_t)m0 * L * 2;
   for (int64_t i = t0; i < n_rec; i += stride) {
     const int4 v = orders[i];
+    const uint32_t written = (uint32_t)bk.slots[m0 + i / O];  // slots used since the clear
+    const bool fresh = written < (uint32_t)O && (uint32_t)(i % O) >= written;
     r.sizes[i] = v.x; r.cids[i] = v.y; r.tids[i] = v.z;
-    r.next[i] = meta_next(v.w); r.prices[i] = meta_price(v.w);
+    r.next[i] = fresh ? -1 : meta_next(v.w); r.prices[i] = meta_price(v.w);
     r.is_bid[i] = (uint8_t)meta_is_bid(v.w);
   }
   for (int64_t i = t0; i < n_lv; i += stride) {
-    const uint32_t eb = levels[2 * i], ea = levels[2 * i + 1];
+    const size_t m = (size_t)m0 + (size_t)(i / L);
+    const int p = (int)(i % L);
+    const Mask128 bm{bk.mask[m], bk.mask[(size_t)N + m]};
+    const Mask128 am_{bk.mask[2 * (size_t)N + m], bk.mask[3 * (size_t)N + m]};
+    const uint32_t eb = mtest(bm, p) ? levels[2 * i] : kEmptyLevel;
+    const uint32_t ea = mtest(am_, p) ? levels[2 * i + 1] : kEmptyLevel;
     r.bid_heads[i] = lv_head(eb); r.bid_tails[i] = lv_tail(eb);
     r.ask_heads[i] = lv_head(ea); r.ask_tails[i] = lv_tail(ea);
   }

@@ -386,6 +386,33 @@ def main():
                           "(one NCCL gather per call, outside the timed matching region)"}
         del out
 
+    # episode boundaries (after every other leg: they clear the book)
+    episode = None
+    if not args.no_extras:
+        half = torch.zeros(N, dtype=torch.bool, device=dev)
+        half[::2] = True
+        res = {}
+        for name, fn in (("clear_quotes_half_ms", lambda: mkt.clear_quotes(half)),
+                         ("reset_ms", mkt.reset)):
+            fn()
+            ee = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            torch.cuda.synchronize()
+            ee[0].record(cur)
+            for _ in range(10):
+                fn()
+            ee[1].record(cur)
+            torch.cuda.synchronize()
+            res[name] = round(ee[0].elapsed_time(ee[1]) / 10, 4)
+        # what the reference's torch fills write (market.cu:699-713, :739-751)
+        ref_reset = 4 * N * L * 4 + N * O * 4 + N * 4 + N * C * 8
+        ref_clear = 4 * N * L * 4 + N * O * 4 + N * 4
+        peak, _ = measured_peak()
+        episode = dict(res, reference_reset_bytes=ref_reset, reference_clear_quotes_bytes=ref_clear,
+                       reference_reset_min_ms=round(ref_reset / (peak * 1e9) * 1e3, 4),
+                       what="Reset / ClearQuotes(every 2nd market) on the stepped book, 10 calls "
+                            "each, CUDA events; reference_*_min_ms = the bytes the reference's "
+                            "fills write at the measured copy bandwidth (a lower bound on its time)")
+
     clk = clocks.stop()
 
     # max over ranks of the timed region
@@ -424,6 +451,8 @@ def main():
             line["events_timed_steps"] = extras["events"]
         if gather:
             line["gather"] = gather
+        if episode:
+            line["episode"] = episode
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(cfg, args, sample=args.cpu_sample)

@@ -102,6 +102,41 @@ def test_reset_and_clear_quotes_match_oracle():
         mkt.clear_quotes(mask.int())
 
 
+@pytest.mark.parametrize("O", [8, 24, 64])
+def test_episodes_of_clears_and_resets_match_oracle(O):
+    """Many short episodes: random ClearQuotes masks every few steps and a
+    Reset every 40, on rings that wrap within an episode (O = 8, 24) or not
+    (O = 64).  Fills, BBOs and the whole exported book are compared after
+    every call, so a stale level entry or record link left behind by a clear
+    would show both in the state (export) and in later matching."""
+    aom = _aom()
+    N, L, F, C, steps = 256, 128, 16, 16, 200
+    q, c = _stream(3, N, steps)
+    mkt = aom.VecMarket(N, L, O, F, C)
+    fills, bbos = mkt.new_fill_batch(), mkt.new_bbo_batch()
+    orc = oracle.OracleMarket(N, L, O, F, C)
+    ofills, obbos = orc.new_fill_batch(), orc.new_bbo_batch()
+    rng = np.random.default_rng(O)
+    for t in range(steps):
+        if t % 40 == 39:
+            mkt.reset()
+            orc.reset()
+        elif t % 7 == 6:
+            m = rng.random(N) < 0.3
+            mkt.clear_quotes(torch.from_numpy(m).to("cuda:0"))
+            orc.clear_quotes(m)
+        if t % 5 == 0:
+            compare_state(mkt, orc, f"before step {t}")
+        mkt.add_two_sided_quotes(q[t, 0], q[t, 1], q[t, 2], q[t, 3], q[t, 4], fills, bbos=bbos)
+        orc.add_two_sided_quotes(*q[t].cpu().numpy(), ofills)
+        orc.get_bbos(obbos)
+        compare_fills(fills, ofills, F, f"step {t}")
+        for name in ("best_bid_prices", "best_bid_sizes", "best_ask_prices", "best_ask_sizes"):
+            np.testing.assert_array_equal(getattr(bbos, name).cpu().numpy(), obbos[name],
+                                          err_msg=f"{name} step {t}")
+    compare_state(mkt, orc, "end")
+
+
 def test_clone_is_deep_and_continues_identically():
     aom = _aom()
     q, _ = _stream(0, 200, 80)

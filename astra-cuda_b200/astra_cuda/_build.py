@@ -20,6 +20,7 @@ CSRC_DIR = os.path.join(ROOT_DIR, "csrc")
 INCLUDE_DIR = os.path.join(REPO_DIR, "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libastra_market.so")
+HEADERS = ("astra_market.h", "astra_trading.h")  # the C ABI
 DIGEST_PATH = LIB_PATH + ".digest"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -30,7 +31,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared"
 def _sources():
     srcs = sorted(os.path.join(CSRC_DIR, f) for f in os.listdir(CSRC_DIR)
                   if f.endswith((".cu", ".cuh", ".h")))
-    srcs.append(os.path.join(INCLUDE_DIR, "astra_market.h"))
+    srcs += [os.path.join(INCLUDE_DIR, h) for h in HEADERS]
     return srcs
 
 

@@ -1,4 +1,5 @@
-"""ctypes binding of the C ABI in ``include/astra_market.h``.
+"""ctypes binding of the C ABI in ``include/astra_market.h`` and
+``include/astra_trading.h``.
 
 The library is the only compute path: if it cannot be loaded (and cannot be
 built because nvcc is absent) importing ``astra_cuda.order_matching`` fails.
@@ -27,6 +28,18 @@ class Market(ctypes.Structure):
     _fields_ = [("dims", Dims), ("device", _i32), ("book", _vp), ("portfolios", _vp)]
 
 
+class TradingDims(ctypes.Structure):
+    _fields_ = [("num_players", _i32), ("steps_per_player", _i32),
+                ("max_contract_value", _i32), ("max_contracts_per_trade", _i32)]
+
+
+class TradingState(ctypes.Structure):
+    _fields_ = [("contract_values", _vp), ("target_positions", _vp),
+                ("player_last_positions", _vp), ("player_contract_over_time", _vp),
+                ("market_contract_over_time", _vp), ("immediate_rewards", _vp),
+                ("rewards_since_last_action", _vp)]
+
+
 class QuoteGen(ctypes.Structure):
     _fields_ = [("seed", ctypes.c_uint64), ("kind", _i32), ("walk", _i32), ("mid_lo", _i32),
                 ("mid_hi", _i32), ("cid_cycle", _i32), ("pad", _i32)]
@@ -50,16 +63,24 @@ _SIGNATURES = {
     "am_check_state": (ctypes.c_int, [_P(Market), _vp, _P(_i32)]),
     "am_generate_quotes": (ctypes.c_int, [_i32, _P(QuoteGen), ctypes.c_uint32, ctypes.c_uint32,
                                           ctypes.c_int64, _i32, _vp, _vp, _vp]),
+    "am_trading_validate": (ctypes.c_int, [_P(Market), _P(TradingDims)]),
+    "am_check_player_moves": (ctypes.c_int, [_P(Market), _vp, _vp, _vp]),
+    "am_apply_player_trading": (ctypes.c_int, [_P(Market), _P(TradingDims), _P(TradingState),
+                                               _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "am_fill_returns": (ctypes.c_int, [_P(Market), _P(TradingDims), _vp, _vp, _vp, _vp]),
 }
+ABI_VERSION = 2
 
 _lib = None
 
 
 def header_functions() -> list[str]:
-    """Names of the functions ``include/astra_market.h`` declares."""
+    """Names of the functions the ABI headers (``include/*.h``) declare."""
     import os
-    with open(os.path.join(_build.INCLUDE_DIR, "astra_market.h")) as f:
-        text = f.read()
+    text = ""
+    for h in _build.HEADERS:
+        with open(os.path.join(_build.INCLUDE_DIR, h)) as f:
+            text += f.read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(am_[a-z0-9_]+)\s*\(", text)))
 
@@ -74,8 +95,8 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
-        if L.am_abi_version() != 1:
-            raise ImportError(f"libastra_market ABI {L.am_abi_version()} != 1")
+        if L.am_abi_version() != ABI_VERSION:
+            raise ImportError(f"libastra_market ABI {L.am_abi_version()} != {ABI_VERSION}")
         _lib = L
     return _lib
 

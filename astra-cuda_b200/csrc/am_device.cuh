@@ -174,6 +174,19 @@ __device__ __forceinline__ int ld_stream(const int32_t* p) {
   asm volatile("ld.global.nc.L1::no_allocate.s32 %0, [%1];" : "=r"(r) : "l"(p));
   return r;
 }
+__device__ __forceinline__ int4 ld_stream_v4(const int4* p) {
+  int4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+// a value this thread updated with red_add: relaxed at gpu scope, so it is
+// read where the reduction was performed (L2), after it
+__device__ __forceinline__ int ld_after_red(const int* p) {
+  int r;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+  return r;
+}
 // write-once outputs (fills, BBO): evict-first
 __device__ __forceinline__ void st_stream(int32_t* p, int v) {
   asm volatile("st.global.cs.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");

@@ -1,4 +1,5 @@
-// C ABI of the matching engine (include/astra_market.h): argument checks,
+// C ABI of the matching engine (include/astra_market.h) and of the fused
+// player-trading step (include/astra_trading.h): argument checks,
 // device guard, launches, error reporting.  No allocation happens here; all
 // buffers are the caller's.
 #include <cuda_runtime.h>
@@ -10,6 +11,7 @@
 
 #include "am_kernels.cuh"
 #include "astra_market.h"
+#include "astra_trading.h"
 
 namespace {
 
@@ -207,7 +209,7 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
     return fail(AM_ERR_INVALID, "BBO outputs must be all NULL or all set");
   DeviceGuard g(mk->device);
   if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
-  am::StepArgs a;
+  am::StepArgs a{};
   a.bk = view(mk);
   a.port = mk->portfolios;
   a.N = d.num_markets; a.L = d.max_price_levels; a.O = d.max_active_orders_per_market;
@@ -395,6 +397,134 @@ int am_generate_quotes(int32_t device, const am_quote_gen* gen, uint32_t step0, 
   am::quotegen_kernel<<<blocks_for(n), am::kBlock, 0, as_stream(stream)>>>(*gen, step0, nsteps,
                                                                            market0, n, mid_state, out);
   return launch_status("generate_quotes");
+}
+
+}  // extern "C"
+
+namespace {
+
+// ---- player-trading step (include/astra_trading.h) ----
+
+int check_trading(const am_market* mk, const am_trading_dims* td) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  if (!td) return fail(AM_ERR_INVALID, "trading dims are NULL");
+  const int P = td->num_players, S = td->steps_per_player, V = td->max_contract_value,
+            T = td->max_contracts_per_trade;
+  if (P < 1 || S < 1 || V < 1 || T < 0)
+    return fail(AM_ERR_INVALID, "players, steps_per_player, max_contract_value >= 1 and "
+                "max_contracts_per_trade >= 0 (P=%d S=%d V=%d T=%d)", P, S, V, T);
+  // high_low_trading.cc:57-69
+  const int64_t O = 2LL * P * S, F = O < 2LL * T ? O : 2LL * T;
+  const am_dims& d = mk->dims;
+  if (d.num_customers != P || d.max_price_levels != V + 1 ||
+      d.max_active_orders_per_market != O || d.max_active_fills_per_market != F)
+    return fail(AM_ERR_INVALID,
+                "market sizes (C=%d L=%d O=%d F=%d) are not the game's (C=%d L=%d O=%lld F=%lld)",
+                d.num_customers, d.max_price_levels, d.max_active_orders_per_market,
+                d.max_active_fills_per_market, P, V + 1, (long long)O, (long long)F);
+  if (d.num_markets < 1) return fail(AM_ERR_INVALID, "num_markets >= 1 (num_markets = %d)", d.num_markets);
+  return AM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int am_trading_validate(const am_market* mk, const am_trading_dims* td) {
+  int rc = check_trading(mk, td);
+  return rc ? rc : ok();
+}
+
+int am_check_player_moves(const am_market* mk, const int32_t* moves, uint32_t* checks,
+                          void* stream) {
+  int rc = check_market(mk);
+  if (rc) return rc;
+  const int N = mk->dims.num_markets;
+  if (N < 1) return fail(AM_ERR_INVALID, "num_markets >= 1 (num_markets = %d)", N);
+  if (!moves || !checks) return fail(AM_ERR_INVALID, "moves and checks must not be NULL");
+  if (!aligned16(moves)) return fail(AM_ERR_INVALID, "moves must be 16-byte aligned");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(checks, 0xFF, 4 * sizeof(uint32_t), s);  // minima start high
+  if (e == cudaSuccess) e = cudaMemsetAsync(checks + 4, 0, 4 * sizeof(uint32_t), s);
+  if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in move checks: %s", cudaGetErrorString(e));
+  am::move_check_kernel<<<grid_stride_blocks(N), am::kBlock, 0, s>>>(
+      reinterpret_cast<const int4*>(moves), N, checks);
+  return launch_status("ApplyPlayerTrading checks");
+}
+
+int am_apply_player_trading(const am_market* mk, const am_trading_dims* td,
+                            const am_trading_state* st, const int32_t* moves,
+                            int32_t trade_move_number, int32_t base_tid, const uint32_t* checks,
+                            int32_t* sticky, int32_t* fills, int32_t* fill_counts, int32_t* bbos,
+                            void* stream) {
+  int rc = check_trading(mk, td);
+  if (rc) return rc;
+  const am_dims& d = mk->dims;
+  const int P = td->num_players, S = td->steps_per_player, t = trade_move_number;
+  if (t < 0 || (int64_t)t >= (int64_t)S * P)  // high_low_trading.cc:251-253
+    return fail(AM_ERR_INVALID, "trade_move_number < steps_per_player_ * num_players_ "
+                "(trade_move_number = %d, steps_per_player_ * num_players_ = %lld)", t,
+                (long long)S * P);
+  if (!st || !st->contract_values || !st->target_positions || !st->player_last_positions ||
+      !st->player_contract_over_time || !st->market_contract_over_time ||
+      !st->immediate_rewards || !st->rewards_since_last_action)
+    return fail(AM_ERR_INVALID, "trading state tensors must not be NULL");
+  if (!moves || !fill_counts || !bbos || (!fills && d.max_active_fills_per_market > 0))
+    return fail(AM_ERR_INVALID, "moves, fills and bbos must not be NULL");
+  if (!aligned16(moves)) return fail(AM_ERR_INVALID, "moves must be 16-byte aligned");
+  if (((reinterpret_cast<uintptr_t>(st->player_last_positions) |
+        reinterpret_cast<uintptr_t>(st->player_contract_over_time) |
+        reinterpret_cast<uintptr_t>(mk->portfolios)) & 7) != 0)
+    return fail(AM_ERR_INVALID, "portfolio and history tensors must be 8-byte aligned");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  const size_t N = (size_t)d.num_markets;
+  am::StepArgs a{};
+  a.bk = view(mk);
+  a.port = mk->portfolios;
+  a.N = d.num_markets; a.L = d.max_price_levels; a.O = d.max_active_orders_per_market;
+  a.F = d.max_active_fills_per_market; a.C = d.num_customers;
+  a.base_tid = base_tid;
+  a.fills = fills; a.fill_counts = fill_counts;
+  a.bbp = bbos; a.bbs = bbos + N; a.bap = bbos + 2 * N; a.bas = bbos + 3 * N;
+  am::TradingArgs& tr = a.tr;
+  tr.moves = reinterpret_cast<const int4*>(moves);
+  tr.player = t % P; tr.t = t; tr.pm = t / P;
+  tr.S = S; tr.V = td->max_contract_value; tr.T = td->max_contracts_per_trade;
+  tr.last_move = (int64_t)t == (int64_t)S * P - 1;
+  tr.checks = checks; tr.sticky = sticky;
+  tr.contract_values = st->contract_values; tr.target_positions = st->target_positions;
+  tr.player_last_positions = st->player_last_positions;
+  tr.player_contract_over_time = st->player_contract_over_time;
+  tr.market_contract_over_time = st->market_contract_over_time;
+  tr.immediate_rewards = st->immediate_rewards;
+  tr.rewards_since_last_action = st->rewards_since_last_action;
+  tr.last_prices = bbos + 4 * N;
+  const int tpb = step_block();
+  const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
+  am::step_kernel<true, false, false, 3, true><<<grid, block, 0, as_stream(stream)>>>(a);
+  return launch_status("ApplyPlayerTrading");
+}
+
+int am_fill_returns(const am_market* mk, const am_trading_dims* td,
+                    const int32_t* contract_values, const int32_t* target_positions,
+                    int32_t* returns, void* stream) {
+  int rc = check_trading(mk, td);
+  if (rc) return rc;
+  if (!contract_values || !target_positions || !returns)
+    return fail(AM_ERR_INVALID, "buffers must not be NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  const int64_t n = (int64_t)mk->dims.num_markets * td->num_players;
+  am::returns_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(
+      mk->portfolios, contract_values, target_positions, mk->dims.num_markets,
+      td->num_players, td->max_contract_value, returns);
+  return launch_status("FillReturns");
 }
 
 }  // extern "C"

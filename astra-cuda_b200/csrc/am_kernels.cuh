@@ -14,6 +14,27 @@
 
 namespace am {
 
+// The player-trading step of the high-low trading game
+// (high_low_trading.cc:247-329): moves in, the game's reward and history
+// tensors out (reference shapes, int32, contiguous).  P = C players.
+struct TradingArgs {
+  const int4* moves;             // [N]{bid_px, ask_px, bid_sz, ask_sz}
+  int player;                    // trade_move_number % P: every order's customer id
+  int t, pm;                     // trade move number, player move number (t / P)
+  int S, V, T;                   // steps per player, max contract value, max contracts per trade
+  bool last_move;                // t == S*P - 1: settlement
+  const uint32_t* checks;        // [8] order-mapped min/max of the move columns, or null
+  int32_t* sticky;               // [9] first failed check: {1, the 8 values}, or null
+  const int32_t* contract_values;      // [N][3]
+  const int32_t* target_positions;     // [N][P]
+  int32_t* player_last_positions;      // [N][P][2]
+  int32_t* player_contract_over_time;  // [N][P][S][6]
+  int32_t* market_contract_over_time;  // [N][P*S][3]
+  int32_t* immediate_rewards;          // [N][P]
+  int32_t* rewards_since_last_action;  // [N][P]
+  int32_t* last_prices;                // [N]
+};
+
 struct StepArgs {
   BookView bk;
   int32_t* port;  // [N][C][2]
@@ -25,6 +46,7 @@ struct StepArgs {
   int32_t *bbp, *bbs, *bap, *bas;
   long long* pos;       // [N][C][2] int64 or null
   unsigned long long* events;  // [5] or null
+  TradingArgs tr;       // read by the trading variant only
 };
 
 // Records whose contents the thread knows without a load: two full head
@@ -149,7 +171,75 @@ __device__ __forceinline__ bool same_sig(const Sig& x, const Sig& y) {
   return x.k == y.k && x.s == y.s;
 }
 
-template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3>
+// The eight value checks of ApplyPlayerTrading (high_low_trading.cc:265-272)
+// on the column minima/maxima of move_check_kernel; true when one fails.
+__device__ __forceinline__ bool moves_fail(const uint32_t* c, int V, int T) {
+  const int mn_bp = (int)(c[0] ^ 0x80000000u), mn_ap = (int)(c[1] ^ 0x80000000u);
+  const int mn_bs = (int)(c[2] ^ 0x80000000u), mn_as = (int)(c[3] ^ 0x80000000u);
+  const int mx_bp = (int)(c[4] ^ 0x80000000u), mx_ap = (int)(c[5] ^ 0x80000000u);
+  const int mx_bs = (int)(c[6] ^ 0x80000000u), mx_as = (int)(c[7] ^ 0x80000000u);
+  return !(mn_bp > 0 && mn_ap > 0 && mx_bp <= V && mx_ap <= V && mn_bs >= 0 && mn_as >= 0 &&
+           mx_bs <= T && mx_as <= T);
+}
+
+__device__ __forceinline__ int wabs(int x) { return x < 0 ? wsub(0, x) : x; }
+
+// ApplyPlayerTrading after the match (high_low_trading.cc:279-328) for market
+// m, in the thread that matched it: last price, history rows, rewards.  The
+// portfolios were updated by this thread's RED adds; ld_after_red reads them
+// back after those.  Integer arithmetic wraps like the reference's int32
+// tensors.
+__device__ __forceinline__ void trading_epilogue(const StepArgs& a, int m, int bp, int ap, int bs,
+                                              int as, int fc, int last_px, int best_bid,
+                                              int best_ask) {
+  const TradingArgs& g = a.tr;
+  const int P = a.C, V = g.V;
+  // BBOBatch::UpdateLastPrices (market.cu:767-786)
+  int last;
+  if (fc > 0) {
+    last = last_px;
+    g.last_prices[m] = last;
+  } else {
+    last = g.last_prices[m];
+  }
+  // market_contract_over_time_[:, t] = best bid, best ask, last price (:290-292)
+  int* mc = g.market_contract_over_time + ((size_t)m * (size_t)(P * g.S) + g.t) * 3;
+  mc[0] = best_bid;
+  mc[1] = best_ask;
+  mc[2] = last;
+  // player_contract_over_time_[:, player, pm, 0:4] = move (:288)
+  int2* mv = reinterpret_cast<int2*>(g.player_contract_over_time +
+                                     (((size_t)m * P + g.player) * g.S + g.pm) * 6);
+  mv[0] = make_int2(bp, ap);
+  mv[1] = make_int2(bs, as);
+  // the acting player's penalties: self trade (:307-308), cheap signalling (:312-316)
+  int pen = wmul(wmul(wadd(min(bs, as), 1), max(wadd(wsub(bp, ap), 1), 0)), V);
+  if (bs == 0 && bp != 1) pen = wadd(pen, V);
+  if (as == 0 && ap != V) pen = wadd(pen, V);
+  const int settle = g.last_move ? g.contract_values[(size_t)m * 3 + 2] : 0;
+  const int2* lrow = reinterpret_cast<const int2*>(g.player_last_positions) + (size_t)m * P;
+  const int* prow = a.port + (size_t)m * P * 2;
+  const int* tgt = g.target_positions + (size_t)m * P;
+  int* imm = g.immediate_rewards + (size_t)m * P;
+  int* rsla = g.rewards_since_last_action + (size_t)m * P;
+  for (int p = 0; p < P; ++p) {
+    const int2 prev = lrow[p];
+    const int cx = ld_after_red(prow + 2 * p), cy = ld_after_red(prow + 2 * p + 1);
+    const int tp = tgt[p];
+    // is_customer * (|prev - target| - |cur - target|) * V + cash_diff (:295-304)
+    int r = tp != 0 ? wmul(wsub(wabs(wsub(prev.x, tp)), wabs(wsub(cx, tp))), V) : 0;
+    r = wadd(r, wsub(cy, prev.y));
+    if (p == g.player) r = wsub(r, pen);
+    if (g.last_move) r = wadd(r, wmul(cx, settle));  // settlement (:318-325)
+    imm[p] = r;
+    rsla[p] = wadd(p == g.player ? 0 : rsla[p], r);  // :279 and :328
+    // player_contract_over_time_[:, :, pm, 4:6] = portfolios (:289)
+    *reinterpret_cast<int2*>(g.player_contract_over_time +
+                             (((size_t)m * P + p) * g.S + g.pm) * 6 + 4) = make_int2(cx, cy);
+  }
+}
+
+template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3, bool kTrading = false>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs a) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   int e_ins = 0, e_fill = 0, e_rm = 0, e_empty = 0;
@@ -158,9 +248,29 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     const size_t N = (size_t)a.N;
     const int L = a.L, O = a.O, F = a.F;
     // ---- round 1: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
-    const int bp = ld_stream(a.bid_px + m), bs = ld_stream(a.bid_sz + m);
-    const int ap = ld_stream(a.ask_px + m), as = ld_stream(a.ask_sz + m);
-    const int cid = ld_stream(a.cids + m);
+    int bp, bs, ap, as, cid;
+    if constexpr (kTrading) {
+      // CopyCustomerPortfoliosTo(player_last_positions_), which the reference
+      // makes before its checks (high_low_trading.cc:257)
+      const TradingArgs& g = a.tr;
+      const int2* prow = reinterpret_cast<const int2*>(a.port) + (size_t)m * a.C;
+      int2* lrow = reinterpret_cast<int2*>(g.player_last_positions) + (size_t)m * a.C;
+      for (int p = 0; p < a.C; ++p) lrow[p] = prow[p];
+      if (g.checks && moves_fail(g.checks, g.V, g.T)) {  // the same answer in every thread
+        if (m == 0 && g.sticky && g.sticky[0] == 0) {
+          for (int k = 0; k < 8; ++k) g.sticky[1 + k] = (int)g.checks[k];
+          g.sticky[0] = 1;
+        }
+        return;
+      }
+      const int4 mv = ld_stream_v4(g.moves + m);  // {bid_px, ask_px, bid_sz, ask_sz}
+      bp = mv.x; ap = mv.y; bs = mv.z; as = mv.w;
+      cid = g.player;
+    } else {
+      bp = ld_stream(a.bid_px + m); bs = ld_stream(a.bid_sz + m);
+      ap = ld_stream(a.ask_px + m); as = ld_stream(a.ask_sz + m);
+      cid = ld_stream(a.cids + m);
+    }
     int ns = a.bk.slots[m];
     Mask128 bm{a.bk.mask[m], a.bk.mask[N + m]};
     Mask128 am_{a.bk.mask[2 * N + m], a.bk.mask[3 * N + m]};
@@ -227,6 +337,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     int eb2_lvl = -2, ea2_lvl = -2;                  // ... of these levels
     int eb2_for = -2, ea2_for = -2;                  // best levels they were fetched for
     int fc = 0;
+    int last_px = 0;  // price of the last fill written (trading variant)
     Sig h1{~0ull, 0}, h2{~0ull, 0};  // signatures of the previous two iterations
     int run = 0;                     // consecutive iterations equal to the one two before
     int rm1 = 0, rm2 = 0;            // removals made by those two iterations
@@ -307,6 +418,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       const int price = bid_is_quote ? meta_price(B.w) : meta_price(A.w);
       const int q = min(B.x, A.x);
       if (fc >= F) { fc = -1; break; }  // market.cu:187-195
+      if constexpr (kTrading) last_px = price;
       int4* fr = reinterpret_cast<int4*>(a.fills + ((size_t)m * (size_t)F + (size_t)fc) * 8);
       // {price, size, taker cid, quoter cid} {quote size, taker tid, quote tid, is_sell_quote}
       st_stream_v4(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y));
@@ -409,6 +521,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       st_stream(a.bap + m, ha ? ba : -1);
       st_stream(a.bas + m, ha ? a_sz : 0);
     }
+    if constexpr (kTrading) trading_epilogue(a, m, bp, ap, bs, as, fc, last_px,
+                                             (bb >= 0 && b_slot >= 0) ? bb : -1,
+                                             (ba < L && a_slot >= 0) ? ba : -1);
   }
   if (kEvents) {
     int e_touch = __popcll(touched);
@@ -475,6 +590,53 @@ __global__ void __launch_bounds__(kBlock) last_price_kernel(int N, int F, int32_
   if (m >= N) return;
   const int c = counts[m];
   if (c > 0 && c <= F) last[m] = fills[((size_t)m * (size_t)F + (size_t)(c - 1)) * 8];
+}
+
+// Column minima (checks[0..3]) and maxima (checks[4..7]) of the moves
+// {bid_px, ask_px, bid_sz, ask_sz}, each int32 x kept as x ^ 0x80000000 so
+// unsigned order is signed order; checks must start at {~0 x4, 0 x4}.  The
+// data of ApplyPlayerTrading's eight checks (high_low_trading.cc:265-272).
+__global__ void __launch_bounds__(kBlock) move_check_kernel(const int4* moves, int N,
+                                                            uint32_t* checks) {
+  uint32_t mn[4] = {~0u, ~0u, ~0u, ~0u}, mx[4] = {0u, 0u, 0u, 0u};
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) {
+    const int4 v = ld_stream_v4(moves + i);
+    const uint32_t u[4] = {(uint32_t)v.x ^ 0x80000000u, (uint32_t)v.y ^ 0x80000000u,
+                           (uint32_t)v.z ^ 0x80000000u, (uint32_t)v.w ^ 0x80000000u};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      mn[k] = min(mn[k], u[k]);
+      mx[k] = max(mx[k], u[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    mn[k] = __reduce_min_sync(0xFFFFFFFFu, mn[k]);
+    mx[k] = __reduce_max_sync(0xFFFFFFFFu, mx[k]);
+  }
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      atomicMin(checks + k, mn[k]);
+      atomicMax(checks + 4 + k, mx[k]);
+    }
+  }
+}
+
+// FillReturns (high_low_trading.cc:345-371): cash + contracts * settlement
+// value - (target != 0) * |contracts - target| * V, int32 with wrap.
+__global__ void __launch_bounds__(kBlock) returns_kernel(const int32_t* port,
+                                                         const int32_t* contract_values,
+                                                         const int32_t* target, int N, int P,
+                                                         int V, int32_t* out) {
+  const int64_t total = (int64_t)N * P;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int cx = port[2 * i], cy = port[2 * i + 1], tp = target[i];
+    int r = wadd(cy, wmul(cx, contract_values[(i / P) * 3 + 2]));
+    if (tp != 0) r = wsub(r, wmul(wabs(wsub(cx, tp)), V));
+    out[i] = r;
+  }
 }
 
 // Constructor state of the order records: a record is zero except its link

@@ -59,7 +59,10 @@ def parse():
     ap.add_argument("--config", type=int, default=4)
     ap.add_argument("--markets", type=int, default=0, help="markets per GPU (default: the config's largest)")
     ap.add_argument("--e2e-steps", type=int, default=100)
-    ap.add_argument("--cpu-sample", type=int, default=8192, help="markets in the CPU baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=262144,
+                    help="markets in the CPU baseline sample (about 10 s of host work at config 4)")
+    ap.add_argument("--trading-envs", type=int, default=1_000_000,
+                    help="environments of the player-trading leg (0: skip it)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip unfused/e2e/replay legs")
     ap.add_argument("--snapshot", default="",
@@ -159,6 +162,7 @@ def cpu_baseline(cfg, args, sample):
     import oracle
     oracle.build()
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    sample = min(sample, max(cfg["markets"]))
     S = max(cfg["steps"], args.warmup + args.steps)
     t_first = S - args.steps
     L, O, F, C = cfg["L"], cfg["O"], cfg["F"], cfg["C"]
@@ -182,6 +186,117 @@ def cpu_baseline(cfg, args, sample):
             "sample": (f"{sample} markets of config {args.config} (global ids 0..{sample - 1}), "
                        f"steps {t_first}..{S - 1} timed after an untimed run of steps 0..{t_first - 1}; "
                        f"AddTwoSidedQuotes + GetBBOs per step, OpenMP over markets")}
+
+
+def reference_pattern_move(g, move):
+    """ApplyPlayerTrading as the reference writes it (high_low_trading.cc:247-329):
+    portfolio copy, eight blocking checks, customer-id tensor, AddTwoSidedQuotes,
+    GetBBOs, UpdateLastPrices and the torch reward ops -- on this package's
+    VecMarket, so the difference to the fused call is the fusion alone."""
+    import torch
+    P, V, T = g.num_players, g.max_contract_value, g.max_contracts_per_trade
+    t = g.trade_move_number
+    player, pm = t % P, t // P
+    g.market.copy_customer_portfolios_to(g.player_last_positions)
+    bid_prices, ask_prices = move[:, 0].contiguous(), move[:, 1].contiguous()
+    bid_sizes, ask_sizes = move[:, 2].contiguous(), move[:, 3].contiguous()
+    customer_ids = torch.ones(g.num_envs, dtype=torch.int32).to(g.device) * player
+    assert torch.min(bid_prices).item() > 0 and torch.min(ask_prices).item() > 0
+    assert torch.max(bid_prices).item() <= V and torch.max(ask_prices).item() <= V
+    assert torch.min(bid_sizes).item() >= 0 and torch.min(ask_sizes).item() >= 0
+    assert torch.max(bid_sizes).item() <= T and torch.max(ask_sizes).item() <= T
+    g.market.add_two_sided_quotes(bid_prices, bid_sizes, ask_prices, ask_sizes, customer_ids,
+                                  g.fill_batch)
+    g.rewards_since_last_action[:, player].zero_()
+    cur = g.market.get_customer_portfolios()
+    g.market.get_bbos(g.bbo_batch)
+    g.bbo_batch.update_last_prices(g.fill_batch)
+    last = g.player_last_positions
+    cash_diff = cur[:, :, 1] - last[:, :, 1]
+    g.player_contract_over_time[:, player, pm, 0:4].copy_(move)
+    g.player_contract_over_time[:, :, pm, 4:].copy_(cur)
+    g.market_contract_over_time[:, t, 0].copy_(g.bbo_batch.best_bid_prices)
+    g.market_contract_over_time[:, t, 1].copy_(g.bbo_batch.best_ask_prices)
+    g.market_contract_over_time[:, t, 2].copy_(g.bbo_batch.last_prices)
+    tgt = g.target_positions
+    prev_diff = torch.abs(last[:, :, 0] - tgt)
+    cur_diff = torch.abs(cur[:, :, 0] - tgt)
+    imm = (tgt != 0) * (prev_diff - cur_diff) * V
+    imm.add_(cash_diff)
+    self_trade = (torch.min(bid_sizes, ask_sizes) + 1) * torch.clamp_min(bid_prices - ask_prices + 1, 0) * V
+    imm[:, player].add_(-self_trade)
+    imm[:, player].add_(-((bid_sizes == 0).int() * (bid_prices != 1).int() * V))
+    imm[:, player].add_(-((ask_sizes == 0).int() * (ask_prices != V).int() * V))
+    if t == g.steps_per_player * P - 1:
+        imm.addcmul_(cur[:, :, 0], g.contract_values[:, 2].unsqueeze(-1))
+    g.immediate_rewards.copy_(imm)
+    g.rewards_since_last_action.add_(g.immediate_rewards)
+    g.market._tid = (g.market._tid + 2 + 2**31) % 2**32 - 2**31
+    g.trade_move_number += 1
+
+
+def trading_leg(dev, envs):
+    """ApplyPlayerTrading per trading move at the game's default sizes (5
+    players, 20 steps each, contract values 1..30, up to 5 contracts): the
+    fused call (deferred and synchronous checks) against the reference's op
+    sequence on the same engine; moves drawn like the reference's
+    high_low_benchmark.py:92-112 (prices U{1..30}, sizes U{0,1}).  The two
+    paths start from the same state and must end bit-identical."""
+    import torch
+    from astra_cuda.high_low_trading import HighLowTradingState
+    P, S, V, T = 5, 20, 30, 5
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    moves = torch.empty((S * P, envs, 4), dtype=torch.int32, device=dev)
+    moves[:, :, :2] = torch.randint(1, V + 1, (S * P, envs, 2), generator=gen, device=dev,
+                                    dtype=torch.int32)
+    moves[:, :, 2:] = torch.randint(0, 2, (S * P, envs, 2), generator=gen, device=dev,
+                                    dtype=torch.int32)
+    cv = torch.randint(1, V + 1, (envs, 2), generator=gen, device=dev, dtype=torch.int32)
+    settle = torch.where(torch.arange(envs, device=dev) % 2 == 1, cv.max(1).values, cv.min(1).values)
+    tgt = torch.zeros((envs, P), dtype=torch.int32, device=dev)
+    tgt[:, 3] = -2
+    tgt[:, 4] = 2
+
+    def episode(g, fn):
+        g.reset()
+        g.contract_values[:, :2].copy_(cv)
+        g.contract_values[:, 2].copy_(settle)
+        g.target_positions.copy_(tgt)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for t in range(S * P):
+            fn(g, moves[t])
+        ev[1].record()
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]) / (S * P)
+
+    out = {"envs": envs, "players": P, "steps_per_player": S, "max_contract_value": V,
+           "max_contracts_per_trade": T, "moves_per_episode": S * P}
+    g = HighLowTradingState(envs, P, S, V, T, device_id=dev.index)
+    r = HighLowTradingState(envs, P, S, V, T, device_id=dev.index)
+    for name, gg, fn in (("fused_deferred", g, lambda x, m: x.apply_player_trading(m, check="deferred")),
+                         ("fused_sync", g, lambda x, m: x.apply_player_trading(m)),
+                         ("reference_pattern", r, reference_pattern_move)):
+        episode(gg, fn)  # warm-up episode
+        out[name + "_ms_per_move"] = round(episode(gg, fn), 4)
+        out[name + "_env_steps_per_s"] = round(envs / (out[name + "_ms_per_move"] * 1e-3))
+    g.check()
+    same = all(torch.equal(getattr(g, k), getattr(r, k)) for k in (
+        "player_last_positions", "player_contract_over_time", "market_contract_over_time",
+        "immediate_rewards", "rewards_since_last_action")) and \
+        torch.equal(g.bbo_batch.storage, r.bbo_batch.storage) and \
+        torch.equal(g.market.get_customer_portfolios(), r.market.get_customer_portfolios())
+    out["fused_equals_reference_pattern"] = bool(same)
+    out["speedup_vs_reference_pattern"] = round(out["reference_pattern_ms_per_move"]
+                                                / out["fused_deferred_ms_per_move"], 2)
+    out["what"] = ("ApplyPlayerTrading per move, CUDA events over the 100 moves of an episode "
+                   "after a warm-up episode; reference_pattern = the reference's op sequence "
+                   "(8 blocking checks, 4 launches of the engine, ~20 torch ops) on this engine")
+    del g, r, moves
+    torch.cuda.empty_cache()
+    return out
 
 
 def config_dict(cfg, args, markets, world):
@@ -386,6 +501,12 @@ def main():
                           "(one NCCL gather per call, outside the timed matching region)"}
         del out
 
+    trading = None
+    if not args.no_extras and world == 1 and args.trading_envs > 0:
+        del fills, bbos, qs
+        torch.cuda.empty_cache()
+        trading = trading_leg(dev, args.trading_envs)
+
     # episode boundaries (after every other leg: they clear the book)
     episode = None
     if not args.no_extras:
@@ -453,6 +574,8 @@ def main():
             line["gather"] = gather
         if episode:
             line["episode"] = episode
+        if trading:
+            line["trading"] = trading
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(cfg, args, sample=args.cpu_sample)

@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define AM_ABI_VERSION 1
+#define AM_ABI_VERSION 2  /* 2: the player-trading entry points of astra_trading.h */
 
 /* Status codes. */
 #define AM_OK 0

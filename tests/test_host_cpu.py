@@ -15,7 +15,7 @@ def test_library_exports_every_header_symbol():
     assert len(names) >= 14
     for n in names:
         assert hasattr(lib, n), n
-    assert lib.am_abi_version() == 1
+    assert lib.am_abi_version() == 2
 
 
 def test_native_dims_validation_without_gpu():

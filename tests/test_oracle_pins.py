@@ -4,6 +4,8 @@ The scenarios (tests/golden/scenarios.py) are the reference's own integration
 test answers (src/tests/integration/test_vec_market.py) plus ring-wrap and
 overflow cases derived by hand from src/order_matching/market.cu.
 """
+import re
+
 import numpy as np
 import pytest
 
@@ -122,3 +124,54 @@ def test_quote_stream_ranges_and_shard_invariance():
         # roughly 10 % of sides absent
         frac = float((bs == 0).mean())
         assert 0.02 < frac < 0.25
+
+
+def test_oracle_trading_episode_known_answers():
+    """The player-trading oracle against the hand-derived episode of
+    tests/golden/trading_scenarios.py (high_low_trading.cc:247-371)."""
+    import oracle_trading
+    from golden import trading_scenarios as ts
+    g = oracle_trading.OracleHighLowTrading(**ts.DIMS)
+    g.contract_values[...] = ts.CONTRACT_VALUES
+    g.target_positions[...] = ts.TARGET_POSITIONS
+    P = ts.DIMS["players"]
+    for t, e in enumerate(ts.EPISODE):
+        move = np.array([e["move"]], np.int32)
+        g.apply_player_trading(move)
+        assert int(g.fills["fill_counts"][0]) == e["count"], t
+        for k, want in enumerate(e.get("fills", [])):
+            for f, v in want.items():
+                got = g.fills[_ORC_FILL[f]][0, k]
+                assert (bool(got) if f == "is_sell_quote" else int(got)) == v, (t, k, f)
+        b = g.bbos
+        assert (int(b["best_bid_prices"][0]), int(b["best_bid_sizes"][0]),
+                int(b["best_ask_prices"][0]), int(b["best_ask_sizes"][0])) == e["bbo"], t
+        assert int(b["last_prices"][0]) == e["last"], t
+        assert [tuple(r) for r in g.market.customer_portfolios[0].tolist()] == e["port"], t
+        assert g.immediate_rewards[0].tolist() == e["imm"], t
+        assert g.rewards_since_last_action[0].tolist() == e["rsla"], t
+        pm = t // P
+        assert g.player_contract_over_time[0, t % P, pm, :4].tolist() == list(e["move"]), t
+        assert [tuple(r) for r in g.player_contract_over_time[0, :, pm, 4:].tolist()] == e["port"], t
+        assert g.market_contract_over_time[0, t].tolist() == [e["bbo"][0], e["bbo"][2], e["last"]], t
+    assert g.fill_returns().tolist() == ts.RETURNS
+    with pytest.raises(oracle_trading.CheckFailed):
+        g.apply_player_trading(np.array([[1, 5, 0, 1]], np.int32))  # the episode is over
+
+
+def test_oracle_trading_checks_in_reference_order():
+    import oracle_trading
+    from golden import trading_scenarios as ts
+    bad = {(0, 5, 1, 1): "min(bid_prices)", (31, 5, 1, 1): "max(bid_prices)",
+           (1, 0, 1, 1): "min(ask_prices)", (1, 31, 1, 1): "max(ask_prices)",
+           (1, 5, -1, 1): "min(bid_sizes)", (1, 5, 6, 1): "max(bid_sizes)",
+           (1, 5, 1, -1): "min(ask_sizes)", (1, 5, 1, 6): "max(ask_sizes)",
+           (0, 31, -1, 6): "min(bid_prices)"}
+    for move, what in bad.items():
+        g = oracle_trading.OracleHighLowTrading(**ts.DIMS)
+        g.market.customer_portfolios[...] = 7
+        with pytest.raises(oracle_trading.CheckFailed, match=re.escape(what)):
+            g.apply_player_trading(np.array([move], np.int32))
+        # the reference copies the portfolios before it checks (:257)
+        assert (g.player_last_positions == 7).all()
+        assert g.trade_move_number == 0 and g.market.global_tid_counter == 0

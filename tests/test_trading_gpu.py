@@ -1,0 +1,208 @@
+"""The fused player-trading step (astra_cuda.high_low_trading, the C ABI of
+include/astra_trading.h) against the hand-derived episode and the CPU oracle
+of high_low_trading.cc:247-371, bit for bit, after every move."""
+import numpy as np
+import pytest
+import torch
+
+import oracle_trading
+from golden import trading_scenarios as ts
+from parity_util import compare_fills
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _hlt():
+    from astra_cuda import high_low_trading
+    return high_low_trading
+
+
+_TENSORS = ("player_last_positions", "player_contract_over_time", "market_contract_over_time",
+            "immediate_rewards", "rewards_since_last_action")
+
+
+def _compare(g, o, where):
+    F = o.market.F
+    compare_fills(g.fill_batch, o.fills, F, where)
+    np.testing.assert_array_equal(g.bbo_batch.storage.cpu().numpy(),
+                                  np.stack([o.bbos[k] for k in (
+                                      "best_bid_prices", "best_bid_sizes", "best_ask_prices",
+                                      "best_ask_sizes", "last_prices")]),
+                                  err_msg=f"BBOBatch {where}")
+    np.testing.assert_array_equal(g.market.get_customer_portfolios().cpu().numpy(),
+                                  o.market.customer_portfolios, err_msg=f"portfolios {where}")
+    for name in _TENSORS:
+        a, b = getattr(g, name).cpu().numpy(), getattr(o, name)
+        if not np.array_equal(a, b):
+            idx = tuple(np.argwhere(a != b)[0])
+            raise AssertionError(f"{name} {where}: first diff at {idx}: gpu {a[idx]} oracle {b[idx]}")
+    assert g.market.global_tid_counter == o.market.global_tid_counter
+    assert g.trade_move_number == o.trade_move_number
+
+
+def test_known_answer_episode():
+    hlt = _hlt()
+    g = hlt.HighLowTradingState(**ts.DIMS)
+    g.contract_values.copy_(torch.tensor(ts.CONTRACT_VALUES, dtype=torch.int32))
+    g.target_positions.copy_(torch.tensor(ts.TARGET_POSITIONS, dtype=torch.int32))
+    P = ts.DIMS["players"]
+    for t, e in enumerate(ts.EPISODE):
+        assert g.current_player() == t % P
+        g.apply_player_trading(torch.tensor([e["move"]], dtype=torch.int32, device="cuda:0"))
+        assert int(g.fill_batch.fill_counts[0]) == e["count"], t
+        for k, want in enumerate(e.get("fills", [])):
+            rec = g.fill_batch.fill_records[0, k].tolist()
+            got = dict(price=rec[0], size=rec[1], customer_id=rec[2], quoter_id=rec[3],
+                       quote_size=rec[4], tid=rec[5], quote_tid=rec[6], is_sell_quote=bool(rec[7]))
+            assert got == want, (t, k)
+        b = g.bbo_batch.storage[:, 0].tolist()
+        assert tuple(b[:4]) == e["bbo"] and b[4] == e["last"], t
+        assert [tuple(r) for r in g.market.get_customer_portfolios()[0].tolist()] == e["port"], t
+        assert g.immediate_rewards[0].tolist() == e["imm"], t
+        assert g.rewards_since_last_action[0].tolist() == e["rsla"], t
+        pm = t // P
+        assert g.player_contract_over_time[0, t % P, pm, :4].tolist() == list(e["move"]), t
+        assert [tuple(r) for r in g.player_contract_over_time[0, :, pm, 4:].tolist()] == e["port"], t
+        assert g.market_contract_over_time[0, t].tolist() == [e["bbo"][0], e["bbo"][2], e["last"]], t
+    assert g.is_terminal() and g.current_player() == hlt.TERMINAL_PLAYER_ID
+    out = torch.zeros((1, P), dtype=torch.int32, device="cuda:0")
+    g.fill_returns(out)
+    assert out.tolist() == ts.RETURNS
+    outf = torch.zeros((1, P), dtype=torch.float32, device="cuda:0")
+    g.fill_returns(outf)
+    assert outf.tolist() == [[float(x) for x in ts.RETURNS[0]]]
+    with pytest.raises(RuntimeError, match="trade_move_number"):
+        g.apply_player_trading(torch.tensor([[1, 5, 0, 1]], dtype=torch.int32, device="cuda:0"))
+
+
+def _random_moves(rng, N, V, T, wide):
+    bp = rng.integers(1, V + 1, N)
+    ap = rng.integers(1, V + 1, N)
+    if wide:  # crossing-heavy: quotes around a per-market mid
+        mid = rng.integers(V // 4, 3 * V // 4, N)
+        bp = np.clip(mid - rng.integers(-2, 5, N), 1, V)
+        ap = np.clip(mid + rng.integers(-2, 5, N), 1, V)
+    bs = rng.integers(0, T + 1, N)
+    as_ = rng.integers(0, T + 1, N)
+    return np.stack([bp, ap, bs, as_], 1).astype(np.int32)
+
+
+@pytest.mark.parametrize("N,P,S,V,T,wide", [(1000, 5, 20, 30, 5, True), (777, 4, 6, 20, 40, True),
+                                            (512, 5, 20, 30, 1, False), (300, 7, 3, 12, 3, True)])
+def test_episodes_match_oracle(N, P, S, V, T, wide):
+    """Two full episodes (Reset between) of random moves; F = min(2PS, 2T)
+    ranges from 2 fill slots (T = 1) to the ring size, so budget overflow
+    (-1 counts) and ring wrap both occur."""
+    hlt = _hlt()
+    rng = np.random.default_rng(N + P)
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    o = oracle_trading.OracleHighLowTrading(N, P, S, V, T)
+    for episode in range(2):
+        cv = rng.integers(1, V + 1, (N, 2)).astype(np.int32)
+        settle = np.where(rng.integers(0, 2, N) == 1, cv.max(1), cv.min(1)).astype(np.int32)
+        cv3 = np.concatenate([cv, settle[:, None]], 1)
+        tgt = rng.integers(-5, 6, (N, P)).astype(np.int32)
+        tgt[:, :min(3, P)] = 0  # the cheater roles have no target
+        g.contract_values.copy_(torch.from_numpy(cv3))
+        g.target_positions.copy_(torch.from_numpy(tgt))
+        o.contract_values[...] = cv3
+        o.target_positions[...] = tgt
+        for t in range(S * P):
+            mv = _random_moves(rng, N, V, T, wide)
+            g.apply_player_trading(torch.from_numpy(mv).to("cuda:0"),
+                                   check="deferred" if t % 3 == 0 else "sync")
+            o.apply_player_trading(mv)
+            _compare(g, o, f"episode {episode} move {t}")
+        g.check()
+        out = torch.empty((N, P), dtype=torch.int32, device="cuda:0")
+        g.fill_returns(out)
+        np.testing.assert_array_equal(out.cpu().numpy(), o.fill_returns())
+        g.reset()
+        o.reset()
+        _compare(g, o, f"after reset {episode}")
+
+
+@pytest.mark.parametrize("col,value,expr", [
+    (0, 0, "torch::min(bid_prices).item<int>() > 0"),
+    (1, -3, "torch::min(ask_prices).item<int>() > 0"),
+    (0, 31, "torch::max(bid_prices).item<int>() <= GetGame()->GetMaxContractValue()"),
+    (1, 99, "torch::max(ask_prices).item<int>() <= GetGame()->GetMaxContractValue()"),
+    (2, -1, "torch::min(bid_sizes).item<int>() >= 0"),
+    (3, -7, "torch::min(ask_sizes).item<int>() >= 0"),
+    (2, 6, "torch::max(bid_sizes).item<int>() <= GetGame()->GetMaxContractsPerTrade()"),
+    (3, 2**31 - 1, "torch::max(ask_sizes).item<int>() <= GetGame()->GetMaxContractsPerTrade()"),
+])
+def test_invalid_moves_raise_like_the_reference(col, value, expr):
+    hlt = _hlt()
+    N, P, S, V, T = 200, 5, 4, 30, 5
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    rng = np.random.default_rng(7)
+    good = torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0")
+    g.apply_player_trading(good)
+    g.apply_player_trading(torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0"))
+    before = {k: getattr(g, k).clone() for k in _TENSORS}
+    port = g.market.get_customer_portfolios().clone()
+    bbo = g.bbo_batch.storage.clone()
+    counts = g.fill_batch.fill_counts.clone()
+    tid, t = g.market.global_tid_counter, g.trade_move_number
+    bad = torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0")
+    bad[N // 2, col] = value
+    with pytest.raises(RuntimeError) as ei:
+        g.apply_player_trading(bad)
+    assert expr in str(ei.value)
+    assert f"= {value}," in str(ei.value)
+    # only the portfolio copy happened (:257 precedes the checks)
+    assert torch.equal(g.player_last_positions, port)
+    for k in _TENSORS[1:]:
+        assert torch.equal(getattr(g, k), before[k]), k
+    assert torch.equal(g.market.get_customer_portfolios(), port)
+    assert torch.equal(g.bbo_batch.storage, bbo) and torch.equal(g.fill_batch.fill_counts, counts)
+    assert g.market.global_tid_counter == tid and g.trade_move_number == t
+    g.apply_player_trading(good)  # the state is still usable
+
+
+def test_deferred_failure_is_raised_by_the_next_check():
+    hlt = _hlt()
+    N, P, S, V, T = 128, 5, 4, 30, 5
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    rng = np.random.default_rng(3)
+    g.apply_player_trading(torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0"),
+                           check="deferred")
+    g.check()  # nothing recorded
+    before = {k: getattr(g, k).clone() for k in _TENSORS[1:]}
+    bad = torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0")
+    bad[3, 0] = 0
+    g.apply_player_trading(bad, check="deferred")  # no exception, no synchronisation
+    for k in _TENSORS[1:]:
+        assert torch.equal(getattr(g, k), before[k]), k
+    assert g.trade_move_number == 2  # a deferred call always advances
+    with pytest.raises(RuntimeError, match=r"torch::min\(bid_prices\)"):
+        g.check()
+    g.check()  # cleared by the read
+    bad2 = bad.clone()
+    g.apply_player_trading(bad2, check="deferred")
+    with pytest.raises(RuntimeError, match=r"torch::min\(bid_prices\)"):  # raised by the next sync call
+        g.apply_player_trading(torch.from_numpy(_random_moves(rng, N, V, T, True)).to("cuda:0"))
+
+
+def test_abi_rejects_a_market_of_other_sizes():
+    import ctypes
+    from astra_cuda import _native
+    hlt = _hlt()
+    g = hlt.HighLowTradingState(64, 5, 4, 30, 5)
+    lib = _native.lib()
+    for dims in [(4, 4, 30, 5), (5, 3, 30, 5), (5, 4, 29, 5), (5, 4, 30, 4), (0, 4, 30, 5)]:
+        td = _native.TradingDims(*dims)
+        assert lib.am_trading_validate(g.market._mkref, ctypes.byref(td)) == _native.AM_ERR_INVALID
+    td = _native.TradingDims(5, 4, 30, 5)
+    assert lib.am_trading_validate(g.market._mkref, ctypes.byref(td)) == 0
+    with pytest.raises(RuntimeError, match="move.size"):
+        g.apply_player_trading(torch.zeros((64, 3), dtype=torch.int32, device="cuda:0"))
+    with pytest.raises(RuntimeError, match="Int"):
+        g.apply_player_trading(torch.ones((64, 4), dtype=torch.int64, device="cuda:0"))

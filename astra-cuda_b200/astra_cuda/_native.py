@@ -40,6 +40,12 @@ class TradingState(ctypes.Structure):
                 ("rewards_since_last_action", _vp)]
 
 
+class ObservationInputs(ctypes.Structure):
+    _fields_ = [("player_permutation", _vp), ("contract_values", _vp),
+                ("contract_high_settle", _vp), ("target_positions", _vp),
+                ("player_contract_over_time", _vp), ("bbos", _vp)]
+
+
 class QuoteGen(ctypes.Structure):
     _fields_ = [("seed", ctypes.c_uint64), ("kind", _i32), ("walk", _i32), ("mid_lo", _i32),
                 ("mid_hi", _i32), ("cid_cycle", _i32), ("pad", _i32)]
@@ -68,6 +74,9 @@ _SIGNATURES = {
     "am_apply_player_trading": (ctypes.c_int, [_P(Market), _P(TradingDims), _P(TradingState),
                                                _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "am_fill_returns": (ctypes.c_int, [_P(Market), _P(TradingDims), _vp, _vp, _vp, _vp]),
+    "am_fill_observation": (ctypes.c_int, [_P(Market), _P(TradingDims), _P(ObservationInputs),
+                                           _i32, _i32, ctypes.c_float, ctypes.c_float,
+                                           ctypes.c_float, _vp, _vp]),
 }
 ABI_VERSION = 2
 

@@ -11,16 +11,23 @@ ops.  ``HighLowTradingState.apply_player_trading`` does the same work in two
 launches of this package's CUDA library (the checks, then the step with its
 epilogue) and at most one host synchronisation (none with ``check="deferred"``).
 
+``fill_observation_tensor`` (FillObservationTensor, :510-601) is one launch
+that writes every element of the float32 observation, where the reference
+zero-fills it and writes it through about thirty indexing and cast ops.
+
 The class holds the tensors the reference's state holds for the trading phase,
 under the reference's member names without the trailing underscore, in the
-reference's shapes (int32, on the market's device).  The game's chance moves
+reference's shapes (on the market's device).  The game's chance moves
 (``ApplyCandidateValues``, ``ApplyHighLowSettle``, ``ApplyPermutation``,
 ``ApplyCustomerSize``, :136-228) are not part of this path: the caller writes
-``contract_values`` [N, 3] and ``target_positions`` [N, P] as those moves would.
+``contract_values`` [N, 3], ``contract_high_settle`` [N] (bool),
+``player_permutation`` [N, P] and ``target_positions`` [N, P] as those moves
+would.
 """
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -89,6 +96,8 @@ class HighLowTradingState:
                "HighLowTradingState")
         z = dict(dtype=torch.int32, device=dev)
         self.contract_values = torch.zeros((N, 3), **z)
+        self.contract_high_settle = torch.zeros((N,), dtype=torch.bool, device=dev)
+        self.player_permutation = torch.zeros((N, P), **z)
         self.target_positions = torch.zeros((N, P), **z)
         self.player_last_positions = torch.zeros((N, P, 2), **z)
         self.player_contract_over_time = torch.zeros((N, P, S, 6), **z)
@@ -221,6 +230,53 @@ class HighLowTradingState:
             self._sticky.zero_()
             _fatal(self._first_failure(h[9:17]) or "deferred move check failed")
 
+    # --- observation (high_low_trading.cc:506-601) ---
+    def observation_tensor_shape(self):
+        """ObservationTensorShape (:506-508): [N, 6 + 1 + 6P + 5]."""
+        return [self.num_envs, 6 + 1 + 6 * self.num_players + 5]
+
+    def fill_observation_tensor(self, player: int, values: torch.Tensor) -> None:
+        """FillObservationTensor (:510-601) for `player` into values, float32
+        [N, 12 + 6P] (other float dtypes receive a copy), in one launch."""
+        P, S = self.num_players, self.steps_per_player
+        _check_op(player, ">=", 0, "player", "0")
+        _check_op(player, "<", P, "player", "GetGame()->NumPlayers()")
+        shape = self.observation_tensor_shape()
+        _check_op(values.dim(), "==", len(shape), "values.sizes().size()", "expected_shape.size()")
+        for i, n in enumerate(shape):
+            _check_op(values.size(i), "==", n, f"values.size({i})", f"expected_shape[{i}]")
+        t = max(0, self.trade_move_number)
+        rnd = t // P
+        if rnd >= S:
+            _fatal(f"index {rnd} is out of bounds for dimension 2 with size {S} "
+                   "(player_contract_over_time_ at the terminal move)")
+        for name in ("player_permutation", "target_positions", "contract_values"):
+            tt = getattr(self, name)
+            if tt.dtype != torch.int32 or not tt.is_contiguous() or tt.device != self.device:
+                _fatal(f"{name} must be a contiguous int32 tensor on device {self.device_id}")
+        hs = self.contract_high_settle
+        if hs.dtype != torch.bool or not hs.is_contiguous() or hs.shape != (self.num_envs,):
+            _fatal("contract_high_settle must be a contiguous bool tensor of shape [num_envs]")
+        self._check_tensors()
+        # the reference computes these on the host: sin/cos in double, then
+        # rounded to float by fill_ (:537-539); round / S in float32 (:554-555)
+        angle = 2.0 * math.pi * player / P
+        frac = float(torch.tensor([float(rnd)], dtype=torch.float32) / S)
+        out = values
+        direct = (out.dtype == torch.float32 and out.is_contiguous() and out.device == self.device)
+        if not direct:
+            out = torch.empty(shape, dtype=torch.float32, device=self.device)
+        inp = _native.ObservationInputs(
+            self.player_permutation.data_ptr(), self.contract_values.data_ptr(),
+            hs.data_ptr(), self.target_positions.data_ptr(),
+            self.player_contract_over_time.data_ptr(), self.bbo_batch.storage.data_ptr())
+        _check(_lib.am_fill_observation(self.market._mkref, ctypes.byref(self._td),
+                                        ctypes.byref(inp), player, t, math.sin(angle),
+                                        math.cos(angle), frac, out.data_ptr(),
+                                        _raw_stream(self.device_id)), "FillObservationTensor")
+        if not direct:
+            values.copy_(out)
+
     # --- reward and return buffers (high_low_trading.cc:331-371) ---
     def fill_rewards(self, reward_buffer: torch.Tensor) -> None:
         """FillRewards: copy immediate_rewards [N, P]."""
@@ -261,7 +317,8 @@ class HighLowTradingState:
 
     # --- DoReset (high_low_trading.cc:373-392), trading tensors ---
     def reset(self) -> None:
-        for t in (self.contract_values, self.target_positions, self.player_last_positions,
+        for t in (self.contract_values, self.contract_high_settle, self.player_permutation,
+                  self.target_positions, self.player_last_positions,
                   self.player_contract_over_time, self.market_contract_over_time,
                   self.immediate_rewards, self.rewards_since_last_action):
             t.zero_()

@@ -527,4 +527,31 @@ int am_fill_returns(const am_market* mk, const am_trading_dims* td,
   return launch_status("FillReturns");
 }
 
+int am_fill_observation(const am_market* mk, const am_trading_dims* td,
+                        const am_observation_inputs* in, int32_t player,
+                        int32_t trade_move_number, float player_sin, float player_cos,
+                        float round_fraction, float* values, void* stream) {
+  int rc = check_trading(mk, td);
+  if (rc) return rc;
+  const int P = td->num_players, S = td->steps_per_player;
+  if (player < 0 || player >= P)  // high_low_trading.cc:512-513
+    return fail(AM_ERR_INVALID, "player < GetGame()->NumPlayers() (player = %d, "
+                "GetGame()->NumPlayers() = %d)", player, P);
+  if (trade_move_number < 0 || trade_move_number / P >= S)
+    return fail(AM_ERR_INVALID, "round %d of trade move %d is outside [0, steps_per_player = %d)",
+                trade_move_number < 0 ? -1 : trade_move_number / P, trade_move_number, S);
+  if (!in || !in->player_permutation || !in->contract_values || !in->contract_high_settle ||
+      !in->target_positions || !in->player_contract_over_time || !in->bbos || !values)
+    return fail(AM_ERR_INVALID, "observation buffers must not be NULL");
+  DeviceGuard g(mk->device);
+  if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  am::ObsArgs o{in->player_permutation, in->contract_values, in->contract_high_settle,
+                in->target_positions, in->player_contract_over_time, in->bbos,
+                mk->dims.num_markets, P, S, player, trade_move_number / P,
+                player_sin, player_cos, round_fraction, values};
+  const int64_t n = (int64_t)mk->dims.num_markets * (12 + 6 * P);
+  am::observation_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(o);
+  return launch_status("FillObservationTensor");
+}
+
 }  // extern "C"

@@ -639,6 +639,70 @@ __global__ void __launch_bounds__(kBlock) returns_kernel(const int32_t* port,
   }
 }
 
+// FillObservationTensor (high_low_trading.cc:510-601) for player `player` at
+// round `round`: values = float32 [N][12 + 6P], one element per thread so the
+// writes are coalesced.  Columns: role one-hot (value cheater, high-low
+// cheater, customer), the player's angle (sin, cos; computed on the host in
+// double and rounded, as the reference's fill_ does), private information,
+// round / S, six history words per player (this round for players before
+// `player`, the last round from `player` on; this round for everyone in round
+// 0 and for the last player; the last round for everyone for player 0), then
+// best bid, best ask, bid size, ask size, last price.  Integers convert with
+// round-to-nearest like the reference's .to(kFloat32).
+struct ObsArgs {
+  const int32_t* player_permutation;         // [N][P]
+  const int32_t* contract_values;            // [N][3]
+  const uint8_t* contract_high_settle;       // [N] bool
+  const int32_t* target_positions;           // [N][P]
+  const int32_t* player_contract_over_time;  // [N][P][S][6]
+  const int32_t* bbos;                       // [5][N]
+  int N, P, S, player, round;
+  float angle_sin, angle_cos, round_fraction;
+  float* values;
+};
+
+__global__ void __launch_bounds__(kBlock) observation_kernel(const ObsArgs o) {
+  const int P = o.P, W = 12 + 6 * P;
+  const int64_t total = (int64_t)o.N * W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / W;
+    const int c = (int)(i - m * W);
+    float v;
+    if (c < 7) {
+      const int perm = o.player_permutation[m * P + o.player];
+      switch (c) {
+        case 0: v = (perm == 0 || perm == 1) ? 1.f : 0.f; break;
+        case 1: v = perm == 2 ? 1.f : 0.f; break;
+        case 2: v = perm > 2 ? 1.f : 0.f; break;
+        case 3: v = o.angle_sin; break;
+        case 4: v = o.angle_cos; break;
+        case 5:
+          v = perm == 0   ? (float)o.contract_values[m * 3]
+              : perm == 1 ? (float)o.contract_values[m * 3 + 1]
+              : perm == 2 ? (o.contract_high_settle[m] ? 1.f : 0.f)
+              : perm > 2  ? (float)o.target_positions[m * P + o.player]
+                          : 0.f;
+          break;
+        default: v = o.round_fraction;
+      }
+    } else if (c < 7 + 6 * P) {
+      const int k = c - 7, q = k / 6, f = k - 6 * (k / 6);
+      int r;
+      if (o.round == 0 || o.player == P - 1) r = o.round;
+      else if (o.player == 0) r = o.round - 1;
+      else r = q < o.player ? o.round : o.round - 1;
+      v = (float)o.player_contract_over_time[((m * P + q) * o.S + r) * 6 + f];
+    } else {
+      // bid px, ask px, bid size, ask size, last price: BBOBatch rows 0, 2, 1, 3, 4
+      const int k = c - 7 - 6 * P;
+      const int row = k == 1 ? 2 : k == 2 ? 1 : k;
+      v = (float)o.bbos[(size_t)row * o.N + m];
+    }
+    o.values[i] = v;
+  }
+}
+
 // Constructor state of the order records: a record is zero except its link
 // (-1) -- market.cu:368-373.
 __global__ void records_kernel(BookView bk, int64_t total) {

@@ -235,6 +235,45 @@ def reference_pattern_move(g, move):
     g.trade_move_number += 1
 
 
+def reference_pattern_observation(g, player, values):
+    """FillObservationTensor as the reference writes it (high_low_trading.cc:510-601):
+    zero fill, role masks, index_put_ of the private information, the history
+    slice (with a cat for players in the middle of a round), five BBO casts."""
+    import math
+    import torch
+    P, S, N = g.num_players, g.steps_per_player, g.num_envs
+    values.fill_(0)
+    perm_ids = g.player_permutation[:, player]
+    values[:, 0] = ((perm_ids == 0) | (perm_ids == 1)).to(torch.float32)
+    values[:, 1] = (perm_ids == 2).to(torch.float32)
+    values[:, 2] = (perm_ids > 2).to(torch.float32)
+    angle = 2.0 * math.pi * player / P
+    values[:, 3].fill_(math.sin(angle))
+    values[:, 4].fill_(math.cos(angle))
+    m0, m1, hl, cu = perm_ids == 0, perm_ids == 1, perm_ids == 2, perm_ids > 2
+    values[m0, 5] = g.contract_values[m0, 0].to(torch.float32)
+    values[m1, 5] = g.contract_values[m1, 1].to(torch.float32)
+    values[hl, 5] = g.contract_high_settle[hl].to(torch.float32)
+    values[cu, 5] = g.target_positions[cu, player].to(torch.float32)
+    r = max(0, g.trade_move_number) // P
+    values[:, 6] = (torch.ones(N).to(torch.float32) * r / S).to(g.device)
+    pc = g.player_contract_over_time
+    if r == 0 or player == P - 1:
+        data = pc[:, :, r, :].reshape(N, P * 6)
+    elif player == 0:
+        data = pc[:, :, r - 1, :].reshape(N, P * 6)
+    else:
+        data = torch.cat([pc[:, :player, r, :], pc[:, player:, r - 1, :]], 1).reshape(N, P * 6)
+    values[:, 7:7 + 6 * P] = data.to(torch.float32)
+    o = 7 + 6 * P
+    b = g.bbo_batch
+    values[:, o] = b.best_bid_prices.to(torch.float32)
+    values[:, o + 1] = b.best_ask_prices.to(torch.float32)
+    values[:, o + 2] = b.best_bid_sizes.to(torch.float32)
+    values[:, o + 3] = b.best_ask_sizes.to(torch.float32)
+    values[:, o + 4] = b.last_prices.to(torch.float32)
+
+
 def trading_leg(dev, envs):
     """ApplyPlayerTrading per trading move at the game's default sizes (5
     players, 20 steps each, contract values 1..30, up to 5 contracts): the
@@ -258,10 +297,14 @@ def trading_leg(dev, envs):
     tgt[:, 3] = -2
     tgt[:, 4] = 2
 
+    perm = torch.argsort(torch.rand((envs, P), generator=gen, device=dev), 1).to(torch.int32)
+
     def episode(g, fn):
         g.reset()
         g.contract_values[:, :2].copy_(cv)
         g.contract_values[:, 2].copy_(settle)
+        g.contract_high_settle.copy_(settle == cv.max(1).values)
+        g.player_permutation.copy_(perm)
         g.target_positions.copy_(tgt)
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -276,13 +319,37 @@ def trading_leg(dev, envs):
            "max_contracts_per_trade": T, "moves_per_episode": S * P}
     g = HighLowTradingState(envs, P, S, V, T, device_id=dev.index)
     r = HighLowTradingState(envs, P, S, V, T, device_id=dev.index)
+    obs_g = torch.empty(g.observation_tensor_shape(), device=dev)
+    obs_r = torch.empty(g.observation_tensor_shape(), device=dev)
+    rew_g = torch.empty((envs, P), dtype=torch.float32, device=dev)
+    rew_r = torch.empty((envs, P), dtype=torch.float32, device=dev)
+    pr_g = torch.empty((envs,), dtype=torch.float32, device=dev)
+    pr_r = torch.empty((envs,), dtype=torch.float32, device=dev)
+
+    def env_step_fused(x, m):  # high_low_benchmark.py:194-214: observe, act, read rewards
+        p = x.current_player()
+        x.fill_observation_tensor(p, obs_g)
+        x.apply_player_trading(m, check="deferred")
+        x.fill_rewards(rew_g)
+        x.fill_rewards_since_last_action(pr_g, p)
+
+    def env_step_reference(x, m):
+        p = x.current_player()
+        reference_pattern_observation(x, p, obs_r)
+        reference_pattern_move(x, m)
+        rew_r.copy_(x.immediate_rewards)
+        pr_r.copy_(x.rewards_since_last_action[:, p])
+
     for name, gg, fn in (("fused_deferred", g, lambda x, m: x.apply_player_trading(m, check="deferred")),
                          ("fused_sync", g, lambda x, m: x.apply_player_trading(m)),
-                         ("reference_pattern", r, reference_pattern_move)):
+                         ("reference_pattern", r, reference_pattern_move),
+                         ("env_step_fused", g, env_step_fused),
+                         ("env_step_reference_pattern", r, env_step_reference)):
         episode(gg, fn)  # warm-up episode
         out[name + "_ms_per_move"] = round(episode(gg, fn), 4)
         out[name + "_env_steps_per_s"] = round(envs / (out[name + "_ms_per_move"] * 1e-3))
     g.check()
+    out["observations_equal"] = bool(torch.equal(obs_g, obs_r)) and bool(torch.equal(pr_g, pr_r))
     same = all(torch.equal(getattr(g, k), getattr(r, k)) for k in (
         "player_last_positions", "player_contract_over_time", "market_contract_over_time",
         "immediate_rewards", "rewards_since_last_action")) and \
@@ -291,10 +358,14 @@ def trading_leg(dev, envs):
     out["fused_equals_reference_pattern"] = bool(same)
     out["speedup_vs_reference_pattern"] = round(out["reference_pattern_ms_per_move"]
                                                 / out["fused_deferred_ms_per_move"], 2)
+    out["env_step_speedup_vs_reference_pattern"] = round(
+        out["env_step_reference_pattern_ms_per_move"] / out["env_step_fused_ms_per_move"], 2)
     out["what"] = ("ApplyPlayerTrading per move, CUDA events over the 100 moves of an episode "
                    "after a warm-up episode; reference_pattern = the reference's op sequence "
-                   "(8 blocking checks, 4 launches of the engine, ~20 torch ops) on this engine")
-    del g, r, moves
+                   "(8 blocking checks, 4 launches of the engine, ~20 torch ops) on this engine; "
+                   "env_step = observation + move + both reward reads, the per-step body of "
+                   "the reference's high_low_benchmark.py")
+    del g, r, moves, obs_g, obs_r
     torch.cuda.empty_cache()
     return out
 

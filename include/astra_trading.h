@@ -86,6 +86,29 @@ int am_fill_returns(const am_market *mk, const am_trading_dims *td,
                     const int32_t *contract_values, const int32_t *target_positions,
                     int32_t *returns, void *stream);
 
+/* What FillObservationTensor reads besides the trading state. */
+typedef struct am_observation_inputs {
+    const int32_t *player_permutation;        /* [N][P]: role of each player (0,1 value
+                                                 cheaters, 2 high-low cheater, >2 customer) */
+    const int32_t *contract_values;           /* [N][3] */
+    const uint8_t *contract_high_settle;      /* [N] bool */
+    const int32_t *target_positions;          /* [N][P] */
+    const int32_t *player_contract_over_time; /* [N][P][S][6] */
+    const int32_t *bbos;                      /* [5][N], the BBOBatch */
+} am_observation_inputs;
+
+/* FillObservationTensor (high_low_trading.cc:510-601) for `player` at trade
+ * move trade_move_number (round = trade_move_number / P, which must be < S)
+ * into values = float32 [N][12 + 6P], every element written (the reference
+ * zero-fills first, then fills every column).  player_sin / player_cos are
+ * sin and cos of 2*pi*player/P computed in double and rounded to float, and
+ * round_fraction is (float)round / (float)S, as the reference computes them
+ * on the host (:537-539, :554-555). */
+int am_fill_observation(const am_market *mk, const am_trading_dims *td,
+                        const am_observation_inputs *in, int32_t player,
+                        int32_t trade_move_number, float player_sin, float player_cos,
+                        float round_fraction, float *values, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

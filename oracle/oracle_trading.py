@@ -10,14 +10,18 @@ market oracle of ``oracle.py``:
   HighLowTradingState constructor  high_low_trading.cc:51-100 (market sizes :57-69)
   ApplyPlayerTrading               high_low_trading.cc:247-329
   FillRewards / ...SinceLastAction high_low_trading.cc:331-343
+  FillObservationTensor            high_low_trading.cc:506-601
   FillReturns                      high_low_trading.cc:345-371
   DoReset (trading tensors)        high_low_trading.cc:373-392
 
 The chance moves (candidate values, settlement side, role permutation,
-customer sizes, :136-228) are not restated: tests set ``contract_values`` and
-``target_positions`` directly, as those moves would.
+customer sizes, :136-228) are not restated: tests set ``contract_values``,
+``contract_high_settle``, ``player_permutation`` and ``target_positions``
+directly, as those moves would.
 """
 from __future__ import annotations
+
+import math
 
 import numpy as np
 
@@ -41,6 +45,8 @@ class OracleHighLowTrading:
         self.fills = self.market.new_fill_batch()
         self.bbos = self.market.new_bbo_batch()
         self.contract_values = np.zeros((N, 3), I32)
+        self.contract_high_settle = np.zeros((N,), np.bool_)
+        self.player_permutation = np.zeros((N, P), I32)
         self.target_positions = np.zeros((N, P), I32)
         self.player_last_positions = np.zeros((N, P, 2), I32)
         self.player_contract_over_time = np.zeros((N, P, S, 6), I32)
@@ -122,6 +128,41 @@ class OracleHighLowTrading:
         self.rewards_since_last_action += self.immediate_rewards
         self.trade_move_number += 1
 
+    def fill_observation(self, player):
+        """FillObservationTensor (high_low_trading.cc:510-601): float32
+        [N, 6 + 1 + 6P + 5]."""
+        N, P, S = self.N, self.P, self.S
+        F32 = np.float32
+        values = np.zeros((N, 6 + 1 + 6 * P + 5), F32)  # :514
+        perm = self.player_permutation[:, player]
+        values[:, 0] = ((perm == 0) | (perm == 1)).astype(F32)  # :529-534
+        values[:, 1] = (perm == 2).astype(F32)
+        values[:, 2] = (perm > 2).astype(F32)
+        angle = 2.0 * math.pi * player / P                        # :536-539
+        values[:, 3] = F32(math.sin(angle))
+        values[:, 4] = F32(math.cos(angle))
+        for mask, src in (((perm == 0), self.contract_values[:, 0].astype(F32)),  # :541-550
+                          ((perm == 1), self.contract_values[:, 1].astype(F32)),
+                          ((perm == 2), self.contract_high_settle.astype(F32)),
+                          ((perm > 2), self.target_positions[:, player].astype(F32))):
+            values[mask, 5] = src[mask]
+        rnd = max(0, self.trade_move_number) // P                 # :552-555
+        values[:, 6] = np.ones(N, F32) * F32(rnd) / F32(S)
+        pcot = self.player_contract_over_time
+        if rnd == 0 or player == P - 1:                           # :558-585
+            data = pcot[:, :, rnd, :]
+        elif player == 0:
+            data = pcot[:, :, rnd - 1, :]
+        else:
+            data = np.concatenate([pcot[:, :player, rnd, :], pcot[:, player:, rnd - 1, :]], 1)
+        values[:, 7:7 + 6 * P] = data.reshape(N, 6 * P).astype(F32)
+        o = 7 + 6 * P                                             # :590-600
+        b = self.bbos
+        for k, key in enumerate(("best_bid_prices", "best_ask_prices", "best_bid_sizes",
+                                 "best_ask_sizes", "last_prices")):
+            values[:, o + k] = b[key].astype(F32)
+        return values
+
     def fill_returns(self):
         """FillReturns (high_low_trading.cc:345-371)."""
         port = self.market.customer_portfolios
@@ -134,7 +175,8 @@ class OracleHighLowTrading:
 
     def reset(self):
         """DoReset (high_low_trading.cc:373-392) for the trading tensors."""
-        for a in (self.contract_values, self.target_positions, self.player_last_positions,
+        for a in (self.contract_values, self.contract_high_settle, self.player_permutation,
+                  self.target_positions, self.player_last_positions,
                   self.player_contract_over_time, self.market_contract_over_time,
                   self.immediate_rewards, self.rewards_since_last_action):
             a[...] = 0

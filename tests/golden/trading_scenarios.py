@@ -74,3 +74,34 @@ EPISODE = [
                      quote_size=1, tid=15, quote_tid=0)]),
 ]
 RETURNS = [[8, -2, 2, -38]]
+
+# FillObservationTensor (high_low_trading.cc:510-601) with roles = player ids
+# (player_permutation [[0, 1, 2, 3]]: players 0, 1 value cheaters, 2 the
+# high-low cheater, 3 the customer), taken before the move `before_move`.
+# Columns: role one-hot (3), sin and cos of 2*pi*player/4 ("SIN", "COS": the
+# double values rounded to float32), private information, round / S, six
+# history words per player (moves and portfolios of the rows the rule at
+# :558-585 picks), best bid, best ask, bid size, ask size, last price.
+#  - before t3, player 3 (round 0: this round's rows; player 3 has not moved,
+#    its portfolio columns are the (0, 0) every move writes); private = target -2.
+#  - before t4, player 0 (round 1, first player: round 0's rows, written last
+#    by t3); private = candidate value 3; round / S = 1/2.
+PERMUTATION = [[0, 1, 2, 3]]
+OBSERVATIONS = [
+    dict(before_move=3, player=3, expect=[
+        0, 0, 1, "SIN", "COS", -2, 0,
+        5, 10, 2, 1, -1, 10, 10, 12, 1, 0, 1, -10, 6, 5, 3, 2, 0, 0, 0, 0, 0, 0, 0, 0,
+        6, -1, 1, 0, 6]),
+    dict(before_move=4, player=0, expect=[
+        1, 0, 0, "SIN", "COS", 3, 0.5,
+        5, 10, 2, 1, 0, 5, 10, 12, 1, 0, 1, -10, 6, 5, 3, 2, 1, -6, 1, 4, 0, 2, -2, 11,
+        5, -1, 1, 0, 5]),
+]
+
+
+def observation_expect(entry, players):
+    import math
+    import numpy as np
+    angle = 2.0 * math.pi * entry["player"] / players
+    sub = {"SIN": float(np.float32(math.sin(angle))), "COS": float(np.float32(math.cos(angle)))}
+    return [sub.get(v, v) if isinstance(v, str) else float(v) for v in entry["expect"]]

@@ -134,8 +134,13 @@ def test_oracle_trading_episode_known_answers():
     g = oracle_trading.OracleHighLowTrading(**ts.DIMS)
     g.contract_values[...] = ts.CONTRACT_VALUES
     g.target_positions[...] = ts.TARGET_POSITIONS
+    g.player_permutation[...] = ts.PERMUTATION
     P = ts.DIMS["players"]
+    obs = {o["before_move"]: o for o in ts.OBSERVATIONS}
     for t, e in enumerate(ts.EPISODE):
+        if t in obs:
+            got = g.fill_observation(obs[t]["player"])[0].tolist()
+            assert got == ts.observation_expect(obs[t], P), t
         move = np.array([e["move"]], np.int32)
         g.apply_player_trading(move)
         assert int(g.fills["fill_counts"][0]) == e["count"], t

@@ -1,6 +1,9 @@
-"""The fused player-trading step (astra_cuda.high_low_trading, the C ABI of
-include/astra_trading.h) against the hand-derived episode and the CPU oracle
-of high_low_trading.cc:247-371, bit for bit, after every move."""
+"""The fused player-trading step and observation writer
+(astra_cuda.high_low_trading, the C ABI of include/astra_trading.h) against the
+hand-derived episode and the CPU oracle of high_low_trading.cc:247-601, bit for
+bit, after every move.  The observation is float32; its tolerance is zero:
+every element is an int32 converted with round-to-nearest or a constant the
+host computes exactly as the reference does."""
 import numpy as np
 import pytest
 import torch
@@ -51,9 +54,15 @@ def test_known_answer_episode():
     g = hlt.HighLowTradingState(**ts.DIMS)
     g.contract_values.copy_(torch.tensor(ts.CONTRACT_VALUES, dtype=torch.int32))
     g.target_positions.copy_(torch.tensor(ts.TARGET_POSITIONS, dtype=torch.int32))
+    g.player_permutation.copy_(torch.tensor(ts.PERMUTATION, dtype=torch.int32))
     P = ts.DIMS["players"]
+    obs = {o["before_move"]: o for o in ts.OBSERVATIONS}
+    values = torch.full(g.observation_tensor_shape(), 7.0, device="cuda:0")
     for t, e in enumerate(ts.EPISODE):
         assert g.current_player() == t % P
+        if t in obs:
+            g.fill_observation_tensor(obs[t]["player"], values)
+            assert values[0].tolist() == ts.observation_expect(obs[t], P), t
         g.apply_player_trading(torch.tensor([e["move"]], dtype=torch.int32, device="cuda:0"))
         assert int(g.fill_batch.fill_counts[0]) == e["count"], t
         for k, want in enumerate(e.get("fills", [])):
@@ -109,11 +118,23 @@ def test_episodes_match_oracle(N, P, S, V, T, wide):
         cv3 = np.concatenate([cv, settle[:, None]], 1)
         tgt = rng.integers(-5, 6, (N, P)).astype(np.int32)
         tgt[:, :min(3, P)] = 0  # the cheater roles have no target
+        perm = np.argsort(rng.random((N, P)), 1).astype(np.int32)
+        hs = rng.integers(0, 2, N).astype(np.bool_)
         g.contract_values.copy_(torch.from_numpy(cv3))
         g.target_positions.copy_(torch.from_numpy(tgt))
+        g.player_permutation.copy_(torch.from_numpy(perm))
+        g.contract_high_settle.copy_(torch.from_numpy(hs))
         o.contract_values[...] = cv3
         o.target_positions[...] = tgt
+        o.player_permutation[...] = perm
+        o.contract_high_settle[...] = hs
+        values = torch.empty(g.observation_tensor_shape(), device="cuda:0")
         for t in range(S * P):
+            # every player's observation before the move, as a rollout would take it
+            for p in ([t % P] if t % 2 else range(P)):
+                g.fill_observation_tensor(p, values)
+                np.testing.assert_array_equal(values.cpu().numpy(), o.fill_observation(p),
+                                              err_msg=f"observation p{p} move {t}")
             mv = _random_moves(rng, N, V, T, wide)
             g.apply_player_trading(torch.from_numpy(mv).to("cuda:0"),
                                    check="deferred" if t % 3 == 0 else "sync")
@@ -206,3 +227,22 @@ def test_abi_rejects_a_market_of_other_sizes():
         g.apply_player_trading(torch.zeros((64, 3), dtype=torch.int32, device="cuda:0"))
     with pytest.raises(RuntimeError, match="Int"):
         g.apply_player_trading(torch.ones((64, 4), dtype=torch.int64, device="cuda:0"))
+
+
+def test_observation_shape_and_player_checks():
+    hlt = _hlt()
+    g = hlt.HighLowTradingState(16, 5, 2, 30, 5)
+    assert g.observation_tensor_shape() == [16, 6 + 1 + 30 + 5]
+    with pytest.raises(RuntimeError, match="player"):
+        g.fill_observation_tensor(5, torch.zeros((16, 42), device="cuda:0"))
+    with pytest.raises(RuntimeError, match="values.size"):
+        g.fill_observation_tensor(0, torch.zeros((16, 41), device="cuda:0"))
+    v64 = torch.zeros((16, 42), dtype=torch.float64, device="cuda:0")
+    g.fill_observation_tensor(0, v64)  # other float dtypes receive a copy
+    assert float(v64[0, 4]) == 1.0  # cos(0)
+    rng = np.random.default_rng(1)
+    for _ in range(10):
+        g.apply_player_trading(torch.from_numpy(_random_moves(rng, 16, 30, 5, True)).to("cuda:0"))
+    assert g.is_terminal()
+    with pytest.raises(RuntimeError, match="out of bounds"):
+        g.fill_observation_tensor(0, torch.zeros((16, 42), device="cuda:0"))

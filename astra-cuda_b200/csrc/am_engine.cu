@@ -549,8 +549,9 @@ int am_fill_observation(const am_market* mk, const am_trading_dims* td,
                 in->target_positions, in->player_contract_over_time, in->bbos,
                 mk->dims.num_markets, P, S, player, trade_move_number / P,
                 player_sin, player_cos, round_fraction, values};
-  const int64_t n = (int64_t)mk->dims.num_markets * (12 + 6 * P);
-  am::observation_kernel<<<grid_stride_blocks(n), am::kBlock, 0, as_stream(stream)>>>(o);
+  const int64_t chunks = ((int64_t)mk->dims.num_markets + am::kObsRows - 1) / am::kObsRows;
+  const unsigned blocks = (unsigned)(chunks < 148 * 8 ? chunks : 148 * 8);
+  am::observation_kernel<<<blocks, am::kBlock, 0, as_stream(stream)>>>(o);
   return launch_status("FillObservationTensor");
 }
 

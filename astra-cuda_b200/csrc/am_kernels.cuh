@@ -661,45 +661,52 @@ struct ObsArgs {
   float* values;
 };
 
+constexpr int kObsRows = 256;  // rows per block chunk: 32-bit index math inside it
+
 __global__ void __launch_bounds__(kBlock) observation_kernel(const ObsArgs o) {
   const int P = o.P, W = 12 + 6 * P;
-  const int64_t total = (int64_t)o.N * W;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / W;
-    const int c = (int)(i - m * W);
-    float v;
-    if (c < 7) {
-      const int perm = o.player_permutation[m * P + o.player];
-      switch (c) {
-        case 0: v = (perm == 0 || perm == 1) ? 1.f : 0.f; break;
-        case 1: v = perm == 2 ? 1.f : 0.f; break;
-        case 2: v = perm > 2 ? 1.f : 0.f; break;
-        case 3: v = o.angle_sin; break;
-        case 4: v = o.angle_cos; break;
-        case 5:
-          v = perm == 0   ? (float)o.contract_values[m * 3]
-              : perm == 1 ? (float)o.contract_values[m * 3 + 1]
-              : perm == 2 ? (o.contract_high_settle[m] ? 1.f : 0.f)
-              : perm > 2  ? (float)o.target_positions[m * P + o.player]
-                          : 0.f;
-          break;
-        default: v = o.round_fraction;
+  for (int64_t m0 = (int64_t)blockIdx.x * kObsRows; m0 < o.N;
+       m0 += (int64_t)gridDim.x * kObsRows) {
+    const uint32_t rows = (uint32_t)min((int64_t)kObsRows, (int64_t)o.N - m0);
+    const uint32_t n = rows * (uint32_t)W;
+    float* out = o.values + m0 * W;
+    for (uint32_t e = threadIdx.x; e < n; e += blockDim.x) {
+      const uint32_t r = e / (uint32_t)W;
+      const int64_t m = m0 + r;
+      const int c = (int)(e - r * (uint32_t)W);
+      float v;
+      if (c < 7) {
+        const int perm = o.player_permutation[m * P + o.player];
+        switch (c) {
+          case 0: v = (perm == 0 || perm == 1) ? 1.f : 0.f; break;
+          case 1: v = perm == 2 ? 1.f : 0.f; break;
+          case 2: v = perm > 2 ? 1.f : 0.f; break;
+          case 3: v = o.angle_sin; break;
+          case 4: v = o.angle_cos; break;
+          case 5:
+            v = perm == 0   ? (float)o.contract_values[m * 3]
+                : perm == 1 ? (float)o.contract_values[m * 3 + 1]
+                : perm == 2 ? (o.contract_high_settle[m] ? 1.f : 0.f)
+                : perm > 2  ? (float)o.target_positions[m * P + o.player]
+                            : 0.f;
+            break;
+          default: v = o.round_fraction;
+        }
+      } else if (c < 7 + 6 * P) {
+        const int k = c - 7, q = k / 6, f = k - 6 * (k / 6);
+        int rd;  // the round whose row player q shows
+        if (o.round == 0 || o.player == P - 1) rd = o.round;
+        else if (o.player == 0) rd = o.round - 1;
+        else rd = q < o.player ? o.round : o.round - 1;
+        v = (float)o.player_contract_over_time[((m * P + q) * o.S + rd) * 6 + f];
+      } else {
+        // bid px, ask px, bid size, ask size, last price: BBOBatch rows 0, 2, 1, 3, 4
+        const int k = c - 7 - 6 * P;
+        const int row = k == 1 ? 2 : k == 2 ? 1 : k;
+        v = (float)o.bbos[(size_t)row * o.N + m];
       }
-    } else if (c < 7 + 6 * P) {
-      const int k = c - 7, q = k / 6, f = k - 6 * (k / 6);
-      int r;
-      if (o.round == 0 || o.player == P - 1) r = o.round;
-      else if (o.player == 0) r = o.round - 1;
-      else r = q < o.player ? o.round : o.round - 1;
-      v = (float)o.player_contract_over_time[((m * P + q) * o.S + r) * 6 + f];
-    } else {
-      // bid px, ask px, bid size, ask size, last price: BBOBatch rows 0, 2, 1, 3, 4
-      const int k = c - 7 - 6 * P;
-      const int row = k == 1 ? 2 : k == 2 ? 1 : k;
-      v = (float)o.bbos[(size_t)row * o.N + m];
+      out[e] = v;
     }
-    o.values[i] = v;
   }
 }
 

@@ -63,6 +63,8 @@ def parse():
                     help="markets in the CPU baseline sample (about 10 s of host work at config 4)")
     ap.add_argument("--trading-envs", type=int, default=1_000_000,
                     help="environments of the player-trading leg (0: skip it)")
+    ap.add_argument("--trading-only", action="store_true",
+                    help="run only the fused trading legs (for profiling)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip unfused/e2e/replay legs")
     ap.add_argument("--snapshot", default="",
@@ -274,7 +276,7 @@ def reference_pattern_observation(g, player, values):
     values[:, o + 4] = b.last_prices.to(torch.float32)
 
 
-def trading_leg(dev, envs):
+def trading_leg(dev, envs, fused_only=False):
     """ApplyPlayerTrading per trading move at the game's default sizes (5
     players, 20 steps each, contract values 1..30, up to 5 contracts): the
     fused call (deferred and synchronous checks) against the reference's op
@@ -340,15 +342,20 @@ def trading_leg(dev, envs):
         rew_r.copy_(x.immediate_rewards)
         pr_r.copy_(x.rewards_since_last_action[:, p])
 
-    for name, gg, fn in (("fused_deferred", g, lambda x, m: x.apply_player_trading(m, check="deferred")),
-                         ("fused_sync", g, lambda x, m: x.apply_player_trading(m)),
-                         ("reference_pattern", r, reference_pattern_move),
-                         ("env_step_fused", g, env_step_fused),
-                         ("env_step_reference_pattern", r, env_step_reference)):
+    legs = [("fused_deferred", g, lambda x, m: x.apply_player_trading(m, check="deferred")),
+            ("fused_sync", g, lambda x, m: x.apply_player_trading(m)),
+            ("reference_pattern", r, reference_pattern_move),
+            ("env_step_fused", g, env_step_fused),
+            ("env_step_reference_pattern", r, env_step_reference)]
+    if fused_only:
+        legs = [legs[0], legs[3]]
+    for name, gg, fn in legs:
         episode(gg, fn)  # warm-up episode
         out[name + "_ms_per_move"] = round(episode(gg, fn), 4)
         out[name + "_env_steps_per_s"] = round(envs / (out[name + "_ms_per_move"] * 1e-3))
     g.check()
+    if fused_only:
+        return out
     out["observations_equal"] = bool(torch.equal(obs_g, obs_r)) and bool(torch.equal(pr_g, pr_r))
     same = all(torch.equal(getattr(g, k), getattr(r, k)) for k in (
         "player_last_positions", "player_contract_over_time", "market_contract_over_time",
@@ -385,6 +392,12 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.trading_only:  # the fused trading legs alone (small profiling runs)
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps({"trading": trading_leg(torch.device("cuda", local), args.trading_envs,
+                                                 fused_only=True)}), flush=True)
+        return
 
     import torch
     import torch.distributed as dist

@@ -37,13 +37,15 @@ class TradingState(ctypes.Structure):
     _fields_ = [("contract_values", _vp), ("target_positions", _vp),
                 ("player_last_positions", _vp), ("player_contract_over_time", _vp),
                 ("market_contract_over_time", _vp), ("immediate_rewards", _vp),
-                ("rewards_since_last_action", _vp)]
+                ("rewards_since_last_action", _vp), ("pcot_stride", ctypes.c_int64 * 4),
+                ("mcot_stride", ctypes.c_int64 * 3)]
 
 
 class ObservationInputs(ctypes.Structure):
     _fields_ = [("player_permutation", _vp), ("contract_values", _vp),
                 ("contract_high_settle", _vp), ("target_positions", _vp),
-                ("player_contract_over_time", _vp), ("bbos", _vp)]
+                ("player_contract_over_time", _vp), ("bbos", _vp),
+                ("pcot_stride", ctypes.c_int64 * 4)]
 
 
 class QuoteGen(ctypes.Structure):

@@ -17,7 +17,11 @@ zero-fills it and writes it through about thirty indexing and cast ops.
 
 The class holds the tensors the reference's state holds for the trading phase,
 under the reference's member names without the trailing underscore, in the
-reference's shapes (on the market's device).  The game's chance moves
+reference's shapes (on the market's device).  ``player_contract_over_time``
+and ``market_contract_over_time`` are strided views of environment-minor
+storage (same shape, same indexing, not ``is_contiguous()``): a move writes
+one step of history for every environment, and in this order those writes are
+contiguous.  The game's chance moves
 (``ApplyCandidateValues``, ``ApplyHighLowSettle``, ``ApplyPermutation``,
 ``ApplyCustomerSize``, :136-228) are not part of this path: the caller writes
 ``contract_values`` [N, 3], ``contract_high_settle`` [N] (bool),
@@ -100,8 +104,11 @@ class HighLowTradingState:
         self.player_permutation = torch.zeros((N, P), **z)
         self.target_positions = torch.zeros((N, P), **z)
         self.player_last_positions = torch.zeros((N, P, 2), **z)
-        self.player_contract_over_time = torch.zeros((N, P, S, 6), **z)
-        self.market_contract_over_time = torch.zeros((N, P * S, 3), **z)
+        # history tensors: the reference's shapes and indexing, stored
+        # environment-minor so that one move's writes (all environments, one
+        # step) are contiguous runs: views of [S][6][P][N] and [P*S][3][N]
+        self.player_contract_over_time = torch.zeros((S, 6, P, N), **z).permute(3, 2, 0, 1)
+        self.market_contract_over_time = torch.zeros((P * S, 3, N), **z).permute(2, 0, 1)
         self.immediate_rewards = torch.zeros((N, P), **z)
         self.rewards_since_last_action = torch.zeros((N, P), **z)
         self.bbo_batch = self.market.new_bbo_batch()
@@ -126,11 +133,12 @@ class HighLowTradingState:
         return self.trade_move_number % self.num_players
 
     def _state_struct(self):
+        pc, mc = self.player_contract_over_time, self.market_contract_over_time
         return _native.TradingState(
             self.contract_values.data_ptr(), self.target_positions.data_ptr(),
-            self.player_last_positions.data_ptr(), self.player_contract_over_time.data_ptr(),
-            self.market_contract_over_time.data_ptr(), self.immediate_rewards.data_ptr(),
-            self.rewards_since_last_action.data_ptr())
+            self.player_last_positions.data_ptr(), pc.data_ptr(), mc.data_ptr(),
+            self.immediate_rewards.data_ptr(), self.rewards_since_last_action.data_ptr(),
+            (ctypes.c_int64 * 4)(*pc.stride()), (ctypes.c_int64 * 3)(*mc.stride()))
 
     def _check_tensors(self):
         N, P, S = self.num_envs, self.num_players, self.steps_per_player
@@ -139,12 +147,14 @@ class HighLowTradingState:
                       player_contract_over_time=(N, P, S, 6),
                       market_contract_over_time=(N, P * S, 3), immediate_rewards=(N, P),
                       rewards_since_last_action=(N, P))
+        strided = ("player_contract_over_time", "market_contract_over_time")
         for name, shape in shapes.items():
             t = getattr(self, name)
             if (tuple(t.shape) != shape or t.dtype != torch.int32 or t.device != self.device
-                    or not t.is_contiguous()):
-                _fatal(f"{name} must be a contiguous int32 tensor of shape {list(shape)} "
-                       f"on device {self.device_id}")
+                    or not (t.is_contiguous() or name in strided)
+                    or (name in strided and min(t.stride()) < 1)):
+                _fatal(f"{name} must be an int32 tensor of shape {list(shape)} on device "
+                       f"{self.device_id}" + ("" if name in strided else ", contiguous"))
 
     def apply_player_trading(self, move: torch.Tensor, *, check: str = "sync") -> None:
         """ApplyPlayerTrading (high_low_trading.cc:247-329) for the current
@@ -266,10 +276,11 @@ class HighLowTradingState:
         direct = (out.dtype == torch.float32 and out.is_contiguous() and out.device == self.device)
         if not direct:
             out = torch.empty(shape, dtype=torch.float32, device=self.device)
+        pc = self.player_contract_over_time
         inp = _native.ObservationInputs(
             self.player_permutation.data_ptr(), self.contract_values.data_ptr(),
-            hs.data_ptr(), self.target_positions.data_ptr(),
-            self.player_contract_over_time.data_ptr(), self.bbo_batch.storage.data_ptr())
+            hs.data_ptr(), self.target_positions.data_ptr(), pc.data_ptr(),
+            self.bbo_batch.storage.data_ptr(), (ctypes.c_int64 * 4)(*pc.stride()))
         _check(_lib.am_fill_observation(self.market._mkref, ctypes.byref(self._td),
                                         ctypes.byref(inp), player, t, math.sin(angle),
                                         math.cos(angle), frac, out.data_ptr(),

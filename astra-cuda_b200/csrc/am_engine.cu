@@ -478,9 +478,12 @@ int am_apply_player_trading(const am_market* mk, const am_trading_dims* td,
     return fail(AM_ERR_INVALID, "moves, fills and bbos must not be NULL");
   if (!aligned16(moves)) return fail(AM_ERR_INVALID, "moves must be 16-byte aligned");
   if (((reinterpret_cast<uintptr_t>(st->player_last_positions) |
-        reinterpret_cast<uintptr_t>(st->player_contract_over_time) |
         reinterpret_cast<uintptr_t>(mk->portfolios)) & 7) != 0)
-    return fail(AM_ERR_INVALID, "portfolio and history tensors must be 8-byte aligned");
+    return fail(AM_ERR_INVALID, "portfolio tensors must be 8-byte aligned");
+  for (int k = 0; k < 4; ++k)
+    if (st->pcot_stride[k] < 1) return fail(AM_ERR_INVALID, "player_contract_over_time strides must be positive");
+  for (int k = 0; k < 3; ++k)
+    if (st->mcot_stride[k] < 1) return fail(AM_ERR_INVALID, "market_contract_over_time strides must be positive");
   DeviceGuard g(mk->device);
   if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
   const size_t N = (size_t)d.num_markets;
@@ -505,6 +508,8 @@ int am_apply_player_trading(const am_market* mk, const am_trading_dims* td,
   tr.immediate_rewards = st->immediate_rewards;
   tr.rewards_since_last_action = st->rewards_since_last_action;
   tr.last_prices = bbos + 4 * N;
+  for (int k = 0; k < 4; ++k) tr.pcot_stride[k] = st->pcot_stride[k];
+  for (int k = 0; k < 3; ++k) tr.mcot_stride[k] = st->mcot_stride[k];
   const int tpb = step_block();
   const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
   am::step_kernel<true, false, false, 3, true><<<grid, block, 0, as_stream(stream)>>>(a);
@@ -545,8 +550,11 @@ int am_fill_observation(const am_market* mk, const am_trading_dims* td,
     return fail(AM_ERR_INVALID, "observation buffers must not be NULL");
   DeviceGuard g(mk->device);
   if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+  for (int k = 0; k < 4; ++k)
+    if (in->pcot_stride[k] < 1) return fail(AM_ERR_INVALID, "player_contract_over_time strides must be positive");
   am::ObsArgs o{in->player_permutation, in->contract_values, in->contract_high_settle,
                 in->target_positions, in->player_contract_over_time, in->bbos,
+                {in->pcot_stride[0], in->pcot_stride[1], in->pcot_stride[2], in->pcot_stride[3]},
                 mk->dims.num_markets, P, S, player, trade_move_number / P,
                 player_sin, player_cos, round_fraction, values};
   const int64_t chunks = ((int64_t)mk->dims.num_markets + am::kObsRows - 1) / am::kObsRows;

@@ -28,11 +28,13 @@ struct TradingArgs {
   const int32_t* contract_values;      // [N][3]
   const int32_t* target_positions;     // [N][P]
   int32_t* player_last_positions;      // [N][P][2]
-  int32_t* player_contract_over_time;  // [N][P][S][6]
-  int32_t* market_contract_over_time;  // [N][P*S][3]
+  int32_t* player_contract_over_time;  // [N][P][S][6] through pcot_stride
+  int32_t* market_contract_over_time;  // [N][P*S][3] through mcot_stride
   int32_t* immediate_rewards;          // [N][P]
   int32_t* rewards_since_last_action;  // [N][P]
   int32_t* last_prices;                // [N]
+  int64_t pcot_stride[4];              // env, player, step, word (elements)
+  int64_t mcot_stride[3];              // env, move, word
 };
 
 struct StepArgs {
@@ -203,15 +205,19 @@ __device__ __forceinline__ void trading_epilogue(const StepArgs& a, int m, int b
     last = g.last_prices[m];
   }
   // market_contract_over_time_[:, t] = best bid, best ask, last price (:290-292)
-  int* mc = g.market_contract_over_time + ((size_t)m * (size_t)(P * g.S) + g.t) * 3;
+  const int64_t* ms = g.mcot_stride;
+  int* mc = g.market_contract_over_time + m * ms[0] + g.t * ms[1];
   mc[0] = best_bid;
-  mc[1] = best_ask;
-  mc[2] = last;
+  mc[ms[2]] = best_ask;
+  mc[2 * ms[2]] = last;
   // player_contract_over_time_[:, player, pm, 0:4] = move (:288)
-  int2* mv = reinterpret_cast<int2*>(g.player_contract_over_time +
-                                     (((size_t)m * P + g.player) * g.S + g.pm) * 6);
-  mv[0] = make_int2(bp, ap);
-  mv[1] = make_int2(bs, as);
+  const int64_t* ps = g.pcot_stride;
+  int* hist = g.player_contract_over_time + m * ps[0] + g.pm * ps[2];
+  int* mv = hist + g.player * ps[1];
+  mv[0] = bp;
+  mv[ps[3]] = ap;
+  mv[2 * ps[3]] = bs;
+  mv[3 * ps[3]] = as;
   // the acting player's penalties: self trade (:307-308), cheap signalling (:312-316)
   int pen = wmul(wmul(wadd(min(bs, as), 1), max(wadd(wsub(bp, ap), 1), 0)), V);
   if (bs == 0 && bp != 1) pen = wadd(pen, V);
@@ -234,8 +240,8 @@ __device__ __forceinline__ void trading_epilogue(const StepArgs& a, int m, int b
     imm[p] = r;
     rsla[p] = wadd(p == g.player ? 0 : rsla[p], r);  // :279 and :328
     // player_contract_over_time_[:, :, pm, 4:6] = portfolios (:289)
-    *reinterpret_cast<int2*>(g.player_contract_over_time +
-                             (((size_t)m * P + p) * g.S + g.pm) * 6 + 4) = make_int2(cx, cy);
+    hist[p * ps[1] + 4 * ps[3]] = cx;
+    hist[p * ps[1] + 5 * ps[3]] = cy;
   }
 }
 
@@ -654,8 +660,9 @@ struct ObsArgs {
   const int32_t* contract_values;            // [N][3]
   const uint8_t* contract_high_settle;       // [N] bool
   const int32_t* target_positions;           // [N][P]
-  const int32_t* player_contract_over_time;  // [N][P][S][6]
+  const int32_t* player_contract_over_time;  // [N][P][S][6] through pcot_stride
   const int32_t* bbos;                       // [5][N]
+  int64_t pcot_stride[4];                    // env, player, step, word
   int N, P, S, player, round;
   float angle_sin, angle_cos, round_fraction;
   float* values;
@@ -698,7 +705,8 @@ __global__ void __launch_bounds__(kBlock) observation_kernel(const ObsArgs o) {
         if (o.round == 0 || o.player == P - 1) rd = o.round;
         else if (o.player == 0) rd = o.round - 1;
         else rd = q < o.player ? o.round : o.round - 1;
-        v = (float)o.player_contract_over_time[((m * P + q) * o.S + rd) * 6 + f];
+        const int64_t* ps = o.pcot_stride;
+        v = (float)o.player_contract_over_time[m * ps[0] + q * ps[1] + rd * ps[2] + f * ps[3]];
       } else {
         // bid px, ask px, bid size, ask size, last price: BBOBatch rows 0, 2, 1, 3, 4
         const int k = c - 7 - 6 * P;

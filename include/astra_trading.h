@@ -34,7 +34,12 @@ typedef struct am_trading_dims {
     int32_t max_contracts_per_trade; /* T */
 } am_trading_dims;
 
-/* The trading-phase tensors of HighLowTradingState (high_low_trading.h:95-110). */
+/* The trading-phase tensors of HighLowTradingState (high_low_trading.h:95-110).
+ * The two history tensors are addressed through element strides, so they may
+ * be the reference's contiguous tensors (player_contract_over_time strides
+ * {P*S*6, S*6, 6, 1}, market_contract_over_time {P*S*3, 3, 1}) or stored
+ * environment-minor (strides {1, N, 6*P*N, P*N} and {1, 3*N, N}), where one
+ * move's history writes are coalesced across environments. */
 typedef struct am_trading_state {
     const int32_t *contract_values;      /* [N][3]: two candidates, settlement value */
     const int32_t *target_positions;     /* [N][P]: customer targets, 0 for others */
@@ -43,6 +48,8 @@ typedef struct am_trading_state {
     int32_t *market_contract_over_time;  /* [N][P*S][3]: best bid, best ask, last price */
     int32_t *immediate_rewards;          /* [N][P] */
     int32_t *rewards_since_last_action;  /* [N][P] */
+    int64_t pcot_stride[4];              /* player_contract_over_time: env, player, step, word */
+    int64_t mcot_stride[3];              /* market_contract_over_time: env, move, word */
 } am_trading_state;
 
 /* Checks that the market has the sizes the game gives it
@@ -93,8 +100,9 @@ typedef struct am_observation_inputs {
     const int32_t *contract_values;           /* [N][3] */
     const uint8_t *contract_high_settle;      /* [N] bool */
     const int32_t *target_positions;          /* [N][P] */
-    const int32_t *player_contract_over_time; /* [N][P][S][6] */
+    const int32_t *player_contract_over_time; /* [N][P][S][6], strides below */
     const int32_t *bbos;                      /* [5][N], the BBOBatch */
+    int64_t pcot_stride[4];                   /* as in am_trading_state */
 } am_observation_inputs;
 
 /* FillObservationTensor (high_low_trading.cc:510-601) for `player` at trade

@@ -102,15 +102,23 @@ def _random_moves(rng, N, V, T, wide):
     return np.stack([bp, ap, bs, as_], 1).astype(np.int32)
 
 
-@pytest.mark.parametrize("N,P,S,V,T,wide", [(1000, 5, 20, 30, 5, True), (777, 4, 6, 20, 40, True),
-                                            (512, 5, 20, 30, 1, False), (300, 7, 3, 12, 3, True)])
-def test_episodes_match_oracle(N, P, S, V, T, wide):
+@pytest.mark.parametrize("N,P,S,V,T,wide,contiguous", [
+    (1000, 5, 20, 30, 5, True, False), (777, 4, 6, 20, 40, True, True),
+    (512, 5, 20, 30, 1, False, False), (300, 7, 3, 12, 3, True, True)])
+def test_episodes_match_oracle(N, P, S, V, T, wide, contiguous):
     """Two full episodes (Reset between) of random moves; F = min(2PS, 2T)
     ranges from 2 fill slots (T = 1) to the ring size, so budget overflow
-    (-1 counts) and ring wrap both occur."""
+    (-1 counts) and ring wrap both occur.  `contiguous` swaps in history
+    tensors in the reference's contiguous layout (the strides a C++ caller
+    passes) for the class's environment-minor views."""
     hlt = _hlt()
     rng = np.random.default_rng(N + P)
     g = hlt.HighLowTradingState(N, P, S, V, T)
+    if contiguous:
+        g.player_contract_over_time = torch.zeros((N, P, S, 6), dtype=torch.int32, device="cuda:0")
+        g.market_contract_over_time = torch.zeros((N, P * S, 3), dtype=torch.int32, device="cuda:0")
+    else:
+        assert not g.player_contract_over_time.is_contiguous()
     o = oracle_trading.OracleHighLowTrading(N, P, S, V, T)
     for episode in range(2):
         cv = rng.integers(1, V + 1, (N, 2)).astype(np.int32)

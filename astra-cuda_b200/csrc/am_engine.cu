@@ -557,9 +557,18 @@ int am_fill_observation(const am_market* mk, const am_trading_dims* td,
                 {in->pcot_stride[0], in->pcot_stride[1], in->pcot_stride[2], in->pcot_stride[3]},
                 mk->dims.num_markets, P, S, player, trade_move_number / P,
                 player_sin, player_cos, round_fraction, values};
-  const int64_t chunks = ((int64_t)mk->dims.num_markets + am::kObsRows - 1) / am::kObsRows;
-  const unsigned blocks = (unsigned)(chunks < 148 * 8 ? chunks : 148 * 8);
-  am::observation_kernel<<<blocks, am::kBlock, 0, as_stream(stream)>>>(o);
+  const int ws = (12 + 6 * P) | 1;
+  if (ws <= am::kObsMaxStride) {
+    const int64_t chunks = ((int64_t)mk->dims.num_markets + am::kObsRowsPerBlock - 1) /
+                           am::kObsRowsPerBlock;
+    const unsigned blocks = (unsigned)(chunks < 148 * 16 ? chunks : 148 * 16);
+    am::observation_rows_kernel<<<blocks, am::kObsRowsPerBlock,
+                                  am::kObsRowsPerBlock * ws * sizeof(float), as_stream(stream)>>>(o);
+  } else {
+    const int64_t chunks = ((int64_t)mk->dims.num_markets + am::kObsRows - 1) / am::kObsRows;
+    const unsigned blocks = (unsigned)(chunks < 148 * 8 ? chunks : 148 * 8);
+    am::observation_kernel<<<blocks, am::kBlock, 0, as_stream(stream)>>>(o);
+  }
   return launch_status("FillObservationTensor");
 }
 

@@ -668,6 +668,65 @@ struct ObsArgs {
   float* values;
 };
 
+// The same observation, one thread per environment: the row is built in
+// shared memory (row stride W | 1 words, so a warp's same-column writes hit 32
+// banks) and the block's rows, contiguous in `values`, are copied out
+// coalesced.  For rows of up to kObsMaxStride words (P <= 14); the
+// element-per-thread kernel below covers any P.
+constexpr int kObsRowsPerBlock = 128;
+constexpr int kObsMaxStride = 96;  // 128 rows x 96 words x 4 B = 48 KB of shared memory
+
+__global__ void __launch_bounds__(kObsRowsPerBlock) observation_rows_kernel(const ObsArgs o) {
+  extern __shared__ float tile[];  // [kObsRowsPerBlock][ws]
+  const int P = o.P, W = 12 + 6 * P, ws = W | 1;
+  const int64_t* ps = o.pcot_stride;
+  for (int64_t m0 = (int64_t)blockIdx.x * kObsRowsPerBlock; m0 < o.N;
+       m0 += (int64_t)gridDim.x * kObsRowsPerBlock) {
+    const int rows = (int)min((int64_t)kObsRowsPerBlock, (int64_t)o.N - m0);
+    if ((int)threadIdx.x < rows) {
+      const int64_t m = m0 + threadIdx.x;
+      float* t = tile + threadIdx.x * ws;
+      const int perm = o.player_permutation[m * P + o.player];
+      t[0] = (perm == 0 || perm == 1) ? 1.f : 0.f;
+      t[1] = perm == 2 ? 1.f : 0.f;
+      t[2] = perm > 2 ? 1.f : 0.f;
+      t[3] = o.angle_sin;
+      t[4] = o.angle_cos;
+      t[5] = perm == 0   ? (float)o.contract_values[m * 3]
+             : perm == 1 ? (float)o.contract_values[m * 3 + 1]
+             : perm == 2 ? (o.contract_high_settle[m] ? 1.f : 0.f)
+             : perm > 2  ? (float)o.target_positions[m * P + o.player]
+                         : 0.f;
+      t[6] = o.round_fraction;
+      for (int q = 0; q < P; ++q) {
+        int rd;  // the round whose row player q shows
+        if (o.round == 0 || o.player == P - 1) rd = o.round;
+        else if (o.player == 0) rd = o.round - 1;
+        else rd = q < o.player ? o.round : o.round - 1;
+        const int32_t* h = o.player_contract_over_time + m * ps[0] + q * ps[1] + rd * ps[2];
+#pragma unroll
+        for (int f = 0; f < 6; ++f) t[7 + 6 * q + f] = (float)h[f * ps[3]];
+      }
+      float* b = t + 7 + 6 * P;  // bid px, ask px, bid size, ask size, last price
+      b[0] = (float)o.bbos[m];
+      b[1] = (float)o.bbos[2 * (size_t)o.N + m];
+      b[2] = (float)o.bbos[(size_t)o.N + m];
+      b[3] = (float)o.bbos[3 * (size_t)o.N + m];
+      b[4] = (float)o.bbos[4 * (size_t)o.N + m];
+    }
+    __syncthreads();
+    float* out = o.values + m0 * W;
+    const int n = rows * W;
+    int r = (int)threadIdx.x / W, c = (int)threadIdx.x - r * W;
+    for (int e = threadIdx.x; e < n; e += kObsRowsPerBlock) {
+      out[e] = tile[r * ws + c];
+      c += kObsRowsPerBlock;
+      while (c >= W) { c -= W; ++r; }
+    }
+    __syncthreads();
+  }
+}
+
 constexpr int kObsRows = 256;  // rows per block chunk: 32-bit index math inside it
 
 __global__ void __launch_bounds__(kBlock) observation_kernel(const ObsArgs o) {

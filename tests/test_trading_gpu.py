@@ -254,3 +254,31 @@ def test_observation_shape_and_player_checks():
     assert g.is_terminal()
     with pytest.raises(RuntimeError, match="out of bounds"):
         g.fill_observation_tensor(0, torch.zeros((16, 42), device="cuda:0"))
+
+
+@pytest.mark.parametrize("P", [14, 15, 16])
+def test_observation_row_kernel_boundary(P):
+    """Rows of up to 96 words (P <= 14) are built in shared memory, wider ones
+    element by element; both against the oracle over a short episode."""
+    hlt = _hlt()
+    N, S, V, T = 300, 2, 10, 2
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    o = oracle_trading.OracleHighLowTrading(N, P, S, V, T)
+    rng = np.random.default_rng(P)
+    perm = np.argsort(rng.random((N, P)), 1).astype(np.int32)
+    tgt = np.where(perm > 2, rng.integers(-3, 4, (N, P)), 0).astype(np.int32)
+    cv = rng.integers(1, V + 1, (N, 3)).astype(np.int32)
+    hs = rng.integers(0, 2, N).astype(np.bool_)
+    for name, a in (("player_permutation", perm), ("target_positions", tgt),
+                    ("contract_values", cv), ("contract_high_settle", hs)):
+        getattr(g, name).copy_(torch.from_numpy(a))
+        getattr(o, name)[...] = a
+    values = torch.empty(g.observation_tensor_shape(), device="cuda:0")
+    for t in range(S * P):
+        for p in (0, t % P, P - 1):
+            g.fill_observation_tensor(p, values)
+            np.testing.assert_array_equal(values.cpu().numpy(), o.fill_observation(p),
+                                          err_msg=f"P {P} move {t} player {p}")
+        mv = _random_moves(rng, N, V, T, True)
+        g.apply_player_trading(torch.from_numpy(mv).to("cuda:0"), check="deferred")
+        o.apply_player_trading(mv)

@@ -452,7 +452,8 @@ int am_check_player_moves(const am_market* mk, const int32_t* moves, uint32_t* c
   cudaError_t e = cudaMemsetAsync(checks, 0xFF, 4 * sizeof(uint32_t), s);  // minima start high
   if (e == cudaSuccess) e = cudaMemsetAsync(checks + 4, 0, 4 * sizeof(uint32_t), s);
   if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in move checks: %s", cudaGetErrorString(e));
-  am::move_check_kernel<<<grid_stride_blocks(N), am::kBlock, 0, s>>>(
+  const int64_t want = ((int64_t)N + am::kBlock - 1) / am::kBlock;
+  am::move_check_kernel<<<(unsigned)(want < 148 * 4 ? want : 148 * 4), am::kBlock, 0, s>>>(
       reinterpret_cast<const int4*>(moves), N, checks);
   return launch_status("ApplyPlayerTrading checks");
 }

@@ -602,8 +602,12 @@ __global__ void __launch_bounds__(kBlock) last_price_kernel(int N, int F, int32_
 // {bid_px, ask_px, bid_sz, ask_sz}, each int32 x kept as x ^ 0x80000000 so
 // unsigned order is signed order; checks must start at {~0 x4, 0 x4}.  The
 // data of ApplyPlayerTrading's eight checks (high_low_trading.cc:265-272).
+// Reduced per warp with __reduce_*_sync, then per block in shared memory, so
+// each block makes 8 atomics: the whole grid's atomics meet on the same 8
+// words, and per-warp atomics there serialised into most of the launch time.
 __global__ void __launch_bounds__(kBlock) move_check_kernel(const int4* moves, int N,
                                                             uint32_t* checks) {
+  __shared__ uint32_t part[kBlock / 32][8];
   uint32_t mn[4] = {~0u, ~0u, ~0u, ~0u}, mx[4] = {0u, 0u, 0u, 0u};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) {
     const int4 v = ld_stream_v4(moves + i);
@@ -615,17 +619,26 @@ __global__ void __launch_bounds__(kBlock) move_check_kernel(const int4* moves, i
       mx[k] = max(mx[k], u[k]);
     }
   }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     mn[k] = __reduce_min_sync(0xFFFFFFFFu, mn[k]);
     mx[k] = __reduce_max_sync(0xFFFFFFFFu, mx[k]);
   }
-  if ((threadIdx.x & 31) == 0) {
+  if (lane == 0) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      atomicMin(checks + k, mn[k]);
-      atomicMax(checks + 4 + k, mx[k]);
+      part[warp][k] = mn[k];
+      part[warp][4 + k] = mx[k];
     }
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    const int k = threadIdx.x;
+    uint32_t r = part[0][k];
+    for (int w = 1; w < kBlock / 32; ++w) r = k < 4 ? min(r, part[w][k]) : max(r, part[w][k]);
+    if (k < 4) atomicMin(checks + k, r);
+    else atomicMax(checks + k, r);
   }
 }
 

@@ -94,3 +94,37 @@ def test_bytes_model_and_configs():
     b = workloads.algorithmic_bytes(1, 128, n_ins=2, n_fill=1, n_rm=1, n_empty=0,
                                     with_bbo=True, n_touch=2, with_pos64=True)
     assert b == 20 + 8 + 4 + 32 + 66 + 101 + 8 + 24 + 32
+
+
+def test_trading_abi_validation_without_gpu():
+    """am_trading_validate and the argument checks of the trading entry points
+    (include/astra_trading.h) run on the host before any device work."""
+    from astra_cuda import _native
+    lib = _native.lib()
+    P, S, V, T = 5, 20, 30, 5
+    dims = _native.Dims(64, V + 1, 2 * P * S, min(2 * P * S, 2 * T), P)
+    mk = _native.Market(dims, 0, 4096, 4096)  # never dereferenced by the checks
+    ok = _native.TradingDims(P, S, V, T)
+    assert lib.am_trading_validate(ctypes.byref(mk), ctypes.byref(ok)) == 0
+    for bad in ((4, S, V, T), (P, S - 1, V, T), (P, S, V - 1, T), (P, S, V, T + 1), (0, S, V, T),
+                (P, S, V, -1)):
+        td = _native.TradingDims(*bad)
+        assert lib.am_trading_validate(ctypes.byref(mk), ctypes.byref(td)) == _native.AM_ERR_INVALID
+        assert _native.last_error()
+    st = _native.TradingState()
+    # trade move out of range, then missing state tensors: both rejected on the host
+    rc = lib.am_apply_player_trading(ctypes.byref(mk), ctypes.byref(ok), ctypes.byref(st), 4096,
+                                     P * S, 0, None, None, 4096, 4096, 4096, None)
+    assert rc == _native.AM_ERR_INVALID and "trade_move_number" in _native.last_error()
+    rc = lib.am_apply_player_trading(ctypes.byref(mk), ctypes.byref(ok), ctypes.byref(st), 4096,
+                                     0, 0, None, None, 4096, 4096, 4096, None)
+    assert rc == _native.AM_ERR_INVALID and "NULL" in _native.last_error()
+    inp = _native.ObservationInputs()
+    rc = lib.am_fill_observation(ctypes.byref(mk), ctypes.byref(ok), ctypes.byref(inp), P, 0,
+                                 0.0, 1.0, 0.0, 4096, None)
+    assert rc == _native.AM_ERR_INVALID and "player" in _native.last_error()
+    rc = lib.am_fill_observation(ctypes.byref(mk), ctypes.byref(ok), ctypes.byref(inp), 0, P * S,
+                                 0.0, 1.0, 0.0, 4096, None)
+    assert rc == _native.AM_ERR_INVALID and "round" in _native.last_error()
+    rc = lib.am_check_player_moves(ctypes.byref(mk), 4100, 4096, None)
+    assert rc == _native.AM_ERR_INVALID and "aligned" in _native.last_error()

@@ -8,20 +8,16 @@
 //                                bit p set <=> the side's level p has a head.
 //                                Market-minor so a warp's 32 markets read and
 //                                write each word as one coalesced 256-byte run.
+//   levels  uint32 [N][L][2]     per level and side {head:int16 | tail:int16<<16}
 //   bbo     int32  [4][N]        best-level head cache: bid head slot, its size,
 //                                ask head slot, its size, as the last step left
 //                                them; slot -1 = unknown.  Derived state: it
 //                                saves loads and makes GetBBOs coalesced.
-//   levels  uint32 [N][L][2]     per level and side {head:int16 | tail:int16<<16}
 //   orders  int4   [N][O]        order record {size, customer id, tid,
 //                                next:int16 | price:uint8<<16 | is_bid<<24}
 //
 // Every access a step makes to a level or an order is a single 4- or 16-byte
 // access inside one 32-byte sector, so each costs one sector of DRAM traffic.
-// The per-market words every step reads and writes (slots, mask, bbo) are one
-// contiguous range, [off_slots, off_levels), which can be given an L2
-// persistence window; the BBO cache and the levels are adjacent because both
-// start as 0xFF bytes.
 //
 // The masks are the authority on which levels are live.  In every state the
 // reference can reach, a level's head is -1 exactly when its tail is, and a
@@ -53,8 +49,8 @@ __host__ __device__ inline Layout layout_of(int64_t N, int64_t L, int64_t O) {
   size_t o = 256;  // the flag word lives at offset 0
   l.off_slots = o;  o = align256(o + 4 * (size_t)N);
   l.off_mask = o;   o = align256(o + 32 * (size_t)N);
-  l.off_bbo = o;    o = align256(o + 16 * (size_t)N);
   l.off_levels = o; o = align256(o + 8 * (size_t)N * (size_t)L);
+  l.off_bbo = o;    o = align256(o + 16 * (size_t)N);  // after the levels: both start at 0xFF
   l.off_orders = o; o = align256(o + 16 * (size_t)N * (size_t)O);
   l.total = o;
   return l;

@@ -7,7 +7,6 @@
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
-#include <mutex>
 #include <string>
 
 #include "am_kernels.cuh"
@@ -142,71 +141,6 @@ int step_min_blocks() {
   return v;
 }
 
-// L2 residency of the per-market words for tuning runs (ASTRA_L2_PERSIST=1;
-// off by default): the step launches carry a persisting access-policy window
-// over [off_slots, off_levels) of the book (slot counters, masks, BBO cache:
-// 52 B per market, read and written by every step), and this process's
-// persisting L2 set-aside is sized once per device for it.  The set-aside
-// belongs to this process's context and ends with it.
-bool step_window(const am_market* mk, cudaAccessPolicyWindow* w) {
-  static const bool on = [] {
-    const char* e = getenv("ASTRA_L2_PERSIST");
-    return e && atoi(e) == 1;
-  }();
-  if (!on || mk->device < 0 || mk->device >= 64) return false;
-  static std::mutex mu;
-  static size_t granted[64] = {};
-  static bool tried[64] = {};
-  const am::Layout l = am::layout_of(mk->dims.num_markets, mk->dims.max_price_levels,
-                                     mk->dims.max_active_orders_per_market);
-  size_t bytes = l.off_levels - l.off_slots;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!tried[mk->device]) {
-    tried[mk->device] = true;
-    int maxp = 0;
-    if (cudaDeviceGetAttribute(&maxp, cudaDevAttrMaxPersistingL2CacheSize, mk->device) ==
-            cudaSuccess && maxp > 0) {
-      const size_t want = bytes < (size_t)maxp ? bytes : (size_t)maxp;
-      if (cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want) == cudaSuccess)
-        granted[mk->device] = want;
-    }
-    cudaGetLastError();  // a refused set-aside leaves the launch without a window
-  }
-  if (!granted[mk->device]) return false;
-  int maxw = 0;
-  if (cudaDeviceGetAttribute(&maxw, cudaDevAttrMaxAccessPolicyWindowSize, mk->device) != cudaSuccess ||
-      maxw <= 0)
-    return false;
-  if (bytes > (size_t)maxw) bytes = (size_t)maxw;
-  w->base_ptr = static_cast<char*>(mk->book) + l.off_slots;
-  w->num_bytes = bytes;
-  const float r = (float)granted[mk->device] / (float)bytes;
-  w->hitRatio = r < 1.f ? r : 1.f;
-  w->hitProp = cudaAccessPropertyPersisting;
-  w->missProp = cudaAccessPropertyStreaming;
-  return true;
-}
-
-template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3, bool kTrading = false>
-void launch_step(dim3 grid, dim3 block, cudaStream_t s, const am::StepArgs& a,
-                 const cudaAccessPolicyWindow* w) {
-  if (!w) {
-    am::step_kernel<kBBO, kPos, kEvents, kMinBlocks, kTrading><<<grid, block, 0, s>>>(a);
-    return;
-  }
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeAccessPolicyWindow;
-  attr[0].val.accessPolicyWindow = *w;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, am::step_kernel<kBBO, kPos, kEvents, kMinBlocks, kTrading>, a);
-}
-
 int check_range(const am_dims& d, int32_t market0, int32_t count) {
   if (market0 < 0 || count < 0 || (int64_t)market0 + count > d.num_markets)
     return fail(AM_ERR_INVALID, "market range [%d, %d) outside [0, %d)", market0,
@@ -245,9 +179,8 @@ int am_book_init(const am_market* mk, void* stream) {
   const am::Layout l = am::layout_of(d.num_markets, d.max_price_levels, d.max_active_orders_per_market);
   char* b = static_cast<char*>(mk->book);
   cudaStream_t s = as_stream(stream);
-  cudaError_t e = cudaMemsetAsync(b, 0, l.off_bbo, s);  // flag, slots, masks
-  // BBO cache (unknown) and levels (empty)
-  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_bbo, 0xFF, l.off_orders - l.off_bbo, s);
+  cudaError_t e = cudaMemsetAsync(b, 0, l.off_levels, s);  // flag, slots, masks
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_levels, 0xFF, l.off_orders - l.off_levels, s);
   if (e == cudaSuccess && d.num_customers > 0 && d.num_markets > 0)
     e = cudaMemsetAsync(mk->portfolios, 0, (size_t)d.num_markets * d.num_customers * 8, s);
   if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in book init: %s", cudaGetErrorString(e));
@@ -293,21 +226,19 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
   const int variant = (n_bbo ? 1 : 0) | (positions ? 2 : 0) | (events ? 4 : 0);
   const int tpb = step_block();
   const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
-  cudaAccessPolicyWindow win;
-  const cudaAccessPolicyWindow* w = step_window(mk, &win) ? &win : nullptr;
   if (variant == 3 && step_min_blocks() == 4) {
-    launch_step<true, true, false, 4>(grid, block, s, a, w);
+    am::step_kernel<true, true, false, 4><<<grid, block, 0, s>>>(a);
     return launch_status("AddTwoSidedQuotes");
   }
   switch (variant) {
-    case 0: launch_step<false, false, false>(grid, block, s, a, w); break;
-    case 1: launch_step<true, false, false>(grid, block, s, a, w); break;
-    case 2: launch_step<false, true, false>(grid, block, s, a, w); break;
-    case 3: launch_step<true, true, false>(grid, block, s, a, w); break;
-    case 4: launch_step<false, false, true>(grid, block, s, a, w); break;
-    case 5: launch_step<true, false, true>(grid, block, s, a, w); break;
-    case 6: launch_step<false, true, true>(grid, block, s, a, w); break;
-    default: launch_step<true, true, true>(grid, block, s, a, w); break;
+    case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
+    case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
+    case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
+    case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
+    case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
+    case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
+    case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
+    default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
   }
   return launch_status("AddTwoSidedQuotes");
 }
@@ -354,8 +285,8 @@ int am_reset(const am_market* mk, void* stream) {
   // cache unknown, portfolios 0; the flag is kept.  Level entries and record
   // links are not rewritten: a clear mask bit reads as an empty level and a
   // record past the counter as next = -1.
-  cudaError_t e = cudaMemsetAsync(b + l.off_slots, 0, l.off_bbo - l.off_slots, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_bbo, 0xFF, l.off_levels - l.off_bbo, s);
+  cudaError_t e = cudaMemsetAsync(b + l.off_slots, 0, l.off_levels - l.off_slots, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + l.off_bbo, 0xFF, l.off_orders - l.off_bbo, s);
   if (e == cudaSuccess && d.num_customers > 0 && d.num_markets > 0)
     e = cudaMemsetAsync(mk->portfolios, 0, (size_t)d.num_markets * d.num_customers * 8, s);
   if (e != cudaSuccess) return fail(AM_ERR_CUDA, "CUDA error in Reset: %s", cudaGetErrorString(e));
@@ -582,9 +513,7 @@ int am_apply_player_trading(const am_market* mk, const am_trading_dims* td,
   for (int k = 0; k < 3; ++k) tr.mcot_stride[k] = st->mcot_stride[k];
   const int tpb = step_block();
   const dim3 grid((unsigned)((d.num_markets + tpb - 1) / tpb)), block(tpb);
-  cudaAccessPolicyWindow win;
-  launch_step<true, false, false, 3, true>(grid, block, as_stream(stream), a,
-                                           step_window(mk, &win) ? &win : nullptr);
+  am::step_kernel<true, false, false, 3, true><<<grid, block, 0, as_stream(stream)>>>(a);
   return launch_status("ApplyPlayerTrading");
 }
 

@@ -184,8 +184,8 @@ class HighLowTradingState:
             _fatal(f"move tensor must be on device {self.device_id}")
         if move.dtype != torch.int32:
             raise RuntimeError(f"expected scalar type Int but found {move.dtype} (move)")
-        if not move.is_contiguous():
-            move = move.contiguous()
+        if not move.is_contiguous() or move.data_ptr() % 16:
+            move = move.contiguous() if not move.is_contiguous() else move.clone()  # rows as int4
         self._check_tensors()
         stream = _raw_stream(self.device_id)
         mk = self.market

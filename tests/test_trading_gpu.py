@@ -282,3 +282,46 @@ def test_observation_row_kernel_boundary(P):
         mv = _random_moves(rng, N, V, T, True)
         g.apply_player_trading(torch.from_numpy(mv).to("cuda:0"), check="deferred")
         o.apply_player_trading(mv)
+
+
+@pytest.mark.parametrize("N,P,S,V,T", [(64, 1, 5, 8, 3), (64, 3, 4, 6, 0), (64, 4, 3, 1, 2)])
+def test_edge_game_shapes_match_oracle(N, P, S, V, T):
+    """One player (every fill a self trade), no fill slots (T = 0: F = 0, every
+    cross overflows to -1), one price level (V = 1: every quote crosses)."""
+    hlt = _hlt()
+    rng = np.random.default_rng(100 + P + T + V)
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    o = oracle_trading.OracleHighLowTrading(N, P, S, V, T)
+    perm = np.argsort(rng.random((N, P)), 1).astype(np.int32)
+    tgt = np.where(perm > 2, rng.integers(-2, 3, (N, P)), 0).astype(np.int32)
+    cv = rng.integers(1, V + 1, (N, 3)).astype(np.int32)
+    for name, a in (("player_permutation", perm), ("target_positions", tgt), ("contract_values", cv)):
+        getattr(g, name).copy_(torch.from_numpy(a))
+        getattr(o, name)[...] = a
+    values = torch.empty(g.observation_tensor_shape(), device="cuda:0")
+    for t in range(S * P):
+        g.fill_observation_tensor(t % P, values)
+        np.testing.assert_array_equal(values.cpu().numpy(), o.fill_observation(t % P))
+        mv = _random_moves(rng, N, V, T, False)
+        g.apply_player_trading(torch.from_numpy(mv).to("cuda:0"))
+        o.apply_player_trading(mv)
+        _compare(g, o, f"move {t}")
+    out = torch.empty((N, P), dtype=torch.int32, device="cuda:0")
+    g.fill_returns(out)
+    np.testing.assert_array_equal(out.cpu().numpy(), o.fill_returns())
+
+
+def test_misaligned_move_rows_are_copied():
+    hlt = _hlt()
+    N, P, S, V, T = 32, 4, 2, 10, 2
+    g = hlt.HighLowTradingState(N, P, S, V, T)
+    o = oracle_trading.OracleHighLowTrading(N, P, S, V, T)
+    rng = np.random.default_rng(9)
+    mv = _random_moves(rng, N, V, T, True)
+    flat = torch.zeros(N * 4 + 1, dtype=torch.int32, device="cuda:0")
+    flat[1:] = torch.from_numpy(mv.reshape(-1)).to("cuda:0")
+    odd = flat[1:].view(N, 4)  # contiguous, rows 4 bytes off a 16-byte boundary
+    assert odd.is_contiguous() and odd.data_ptr() % 16 != 0
+    g.apply_player_trading(odd)
+    o.apply_player_trading(mv)
+    _compare(g, o, "misaligned move")

@@ -515,37 +515,27 @@ def main():
         dq = torch.empty((2, 5, N), dtype=torch.int32, device=dev)
         stage = torch.empty((2, N), dtype=torch.int32, device=dev)  # fill counts on their way out
         hcounts = torch.empty((KE, N), dtype=torch.int32).pin_memory()
-        # two H2D streams, each copying half of a step's quotes: two copy
-        # engines move more over PCIe than one (about 50 against 46 GB/s here)
-        h2d_s = [torch.cuda.Stream(dev) for _ in range(2)]
-        d2h_s = torch.cuda.Stream(dev)
-        half = (5 * N) // 2
-        parts = ((0, half), (half, 5 * N))
-        h2d_done = [[torch.cuda.Event() for _ in range(2)] for _ in range(2)]
+        h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
         step_done = [torch.cuda.Event() for _ in range(2)]
         staged = [torch.cuda.Event() for _ in range(2)]
         d2h_done = [torch.cuda.Event() for _ in range(2)]
-
-        def h2d(i, b, after=None):
-            src, dst = hq[i].view(-1), dq[b].view(-1)
-            for k, (lo, hi) in enumerate(parts):
-                with torch.cuda.stream(h2d_s[k]):
-                    if after is not None:
-                        h2d_s[k].wait_event(after)
-                    dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
-                    h2d_done[b][k].record(h2d_s[k])
-
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        h2d(0, 0)
+        with torch.cuda.stream(h2d_s):
+            dq[0].copy_(hq[0], non_blocking=True)
+            h2d_done[0].record(h2d_s)
         for i in range(KE):
             b = i % 2
             if i + 1 < KE:  # the next step's quotes cross PCIe while this step runs
-                h2d(i + 1, 1 - b, step_done[1 - b] if i >= 1 else None)
-            for k in range(2):
-                cur.wait_event(h2d_done[b][k])
+                with torch.cuda.stream(h2d_s):
+                    if i >= 1:
+                        h2d_s.wait_event(step_done[1 - b])
+                    dq[1 - b].copy_(hq[i + 1], non_blocking=True)
+                    h2d_done[1 - b].record(h2d_s)
+            cur.wait_event(h2d_done[b])
             step(dq[b])
             step_done[b].record(cur)
             if i >= 2:
@@ -565,9 +555,8 @@ def main():
         e2e = {"value": N * world * KE / el, "unit": UNIT, "h2d_bytes_per_step": 5 * 4 * N,
                "d2h_bytes_per_step": 4 * N, "steps": KE, "ms_per_step": 1e3 * el / KE,
                "note": "wall clock per rank (max over ranks); each step's quotes copied H2D from "
-                       "pinned host memory one step ahead, in two halves on two copy streams; "
-                       "each step's fill counts staged on the device and copied D2H on a "
-                       "third stream"}
+                       "pinned host memory on a copy stream one step ahead; each step's fill "
+                       "counts staged on the device and copied D2H on a second stream"}
         del hq, hcounts
 
     gather = None

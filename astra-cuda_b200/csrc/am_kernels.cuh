@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
   if (m < a.N) {
     const size_t N = (size_t)a.N;
     const int L = a.L, O = a.O, F = a.F;
-    // ---- round 1: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
+    // ---- first round trip: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
     int bp, bs, ap, as, cid;
     if constexpr (kTrading) {
       // CopyCustomerPortfoliosTo(player_last_positions_), which the reference
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     const bool add_a = as > 0 && ap < L && ap >= 0;
     const int ob = mhigh(bm), oa = mlow(am_, L);  // best levels before inserting
 
-    // ---- round 2: everything the inserts and the first match need ----
+    // ---- second round trip: everything the inserts and the first match need ----
     // After inserting, the best bid is max(ob, bp) and the best ask min(oa, ap),
     // so these four entries cover both; the cached head record of the best
     // level a new quote crosses is fetched at the same time.

@@ -298,17 +298,11 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     // ---- second round trip: everything the inserts and the first match need ----
     // After inserting, the best bid is max(ob, bp) and the best ask min(oa, ap),
     // so these four entries cover both; the cached head record of the best
-    // level a new quote crosses is fetched at the same time.  When the book
-    // will not cross, an old best level is untouched by the step and its head
-    // is in the BBO cache, so its entry is loaded only if the cache is empty.
-    const int nbb = (add_b && bp > ob) ? bp : ob, nba = (add_a && ap < oa) ? ap : oa;
-    const bool crossing = nbb >= 0 && nba < L && nbb >= nba;  // the match loop will run
-    const bool need_bo = ob >= 0 && !(add_b && ob == bp) && (crossing || (nbb == ob && k.cbh < 0));
-    const bool need_ao = oa < L && !(add_a && oa == ap) && (crossing || (nba == oa && k.cah < 0));
+    // level a new quote crosses is fetched at the same time.
     uint32_t eb_ins = (add_b && mtest(bm, bp)) ? lv[2 * bp] : kEmptyLevel;
     uint32_t ea_ins = (add_a && mtest(am_, ap)) ? lv[2 * ap + 1] : kEmptyLevel;
-    const uint32_t eb_old = need_bo ? lv[2 * ob] : kEmptyLevel;
-    const uint32_t ea_old = need_ao ? lv[2 * oa + 1] : kEmptyLevel;
+    const uint32_t eb_old = (ob >= 0 && !(add_b && ob == bp)) ? lv[2 * ob] : kEmptyLevel;
+    const uint32_t ea_old = (oa < L && !(add_a && oa == ap)) ? lv[2 * oa + 1] : kEmptyLevel;
     int4 PB = make_int4(0, 0, 0, 0), PA = PB;  // speculative head records ...
     int pb = -1, pa = -1;                      // ... of these slots (-1: none)
     if (add_a && ob >= 0 && ap <= ob && (uint32_t)k.cbh < (uint32_t)O) {
@@ -344,9 +338,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     int bb = mhigh(bm), ba = mlow(am_, L);
     uint32_t eb = (add_b && bb == bp) ? eb_ins : eb_old;
     uint32_t ea = (add_a && ba == ap) ? ea_ins : ea_old;
-    // level whose entry eb / ea holds (-2: none)
-    int eb_lvl = ((add_b && bb == bp) || need_bo) ? bb : -2;
-    int ea_lvl = ((add_a && ba == ap) || need_ao) ? ba : -2;
+    int eb_lvl = bb, ea_lvl = ba;  // level whose entry eb / ea holds (-2: none)
     uint32_t eb2 = kEmptyLevel, ea2 = kEmptyLevel;  // next-best entries, prefetched ...
     int eb2_lvl = -2, ea2_lvl = -2;                  // ... of these levels
     int eb2_for = -2, ea2_for = -2;                  // best levels they were fetched for
@@ -505,10 +497,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     // output is asked for).
     int b_slot = -1, b_sz = 0, a_slot = -1, a_sz = 0;
     if (bb >= 0) {
-      int h;
-      if (eb_lvl == bb) h = lv_head(eb);
-      else if (!crossing && bb == ob && k.cbh >= 0) h = k.cbh;  // untouched old best
-      else h = lv_head(bb == eb2_lvl ? eb2 : lv[2 * bb]);
+      if (eb_lvl != bb) eb = (bb == eb2_lvl) ? eb2 : lv[2 * bb];
+      const int h = lv_head(eb);
       if ((uint32_t)h < (uint32_t)O) {
         if (known_size(k, h, b_sz)) b_slot = h;
         else if (kBBO) { b_sz = ld_rec_size(rec + h); b_slot = h; }
@@ -517,10 +507,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       }
     }
     if (ba < L) {
-      int h;
-      if (ea_lvl == ba) h = lv_head(ea);
-      else if (!crossing && ba == oa && k.cah >= 0) h = k.cah;  // untouched old best
-      else h = lv_head(ba == ea2_lvl ? ea2 : lv[2 * ba + 1]);
+      if (ea_lvl != ba) ea = (ba == ea2_lvl) ? ea2 : lv[2 * ba + 1];
+      const int h = lv_head(ea);
       if ((uint32_t)h < (uint32_t)O) {
         if (known_size(k, h, a_sz)) a_slot = h;
         else if (kBBO) { a_sz = ld_rec_size(rec + h); a_slot = h; }

@@ -180,3 +180,50 @@ def test_oracle_trading_checks_in_reference_order():
         # the reference copies the portfolios before it checks (:257)
         assert (g.player_last_positions == 7).all()
         assert g.trade_move_number == 0 and g.market.global_tid_counter == 0
+
+
+def test_oracle_reset_and_last_price_scenario():
+    """market_tests.cu:671-750 (TestResetAndLastPrice), answers derived by hand
+    from market.cu: last prices survive VecMarket::Reset and steps without
+    fills; BBOBatch::Reset zeroes them (market.cu:788-796; the C++ test's
+    NULL_INDEX expectation there is stale); then each market fills twice: the
+    new bid first meets the resting ask (the older order sets the price: 35 /
+    45), then the new ask, against which the new bid is the resting order
+    (40 / 50), so the last prices are 40 and 50."""
+    m = oracle.OracleMarket(2, 128, 1024, 512, 16)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    A = lambda *x: np.array(x, np.int32)  # noqa: E731
+    m.add_two_sided_quotes(A(45, 55), A(100, 200), A(45, 55), A(100, 200), A(0, 0), f)
+    m.update_last_prices(b, f)
+    assert b["last_prices"].tolist() == [45, 55]
+    m.reset()
+    assert b["last_prices"].tolist() == [45, 55] and m.global_tid_counter == 0
+    m.add_two_sided_quotes(A(30, 40), A(50, 100), A(35, 45), A(50, 100), A(0, 0), f)
+    m.update_last_prices(b, f)
+    assert f["fill_counts"].tolist() == [0, 0] and b["last_prices"].tolist() == [45, 55]
+    for v in b.values():  # BBOBatch::Reset
+        v[...] = 0
+    m.add_two_sided_quotes(A(40, 50), A(75, 125), A(35, 45), A(75, 125), A(1, 1), f)
+    m.update_last_prices(b, f)
+    assert f["fill_counts"].tolist() == [2, 2]
+    assert f["fill_prices"][:, :2].tolist() == [[35, 40], [45, 50]]
+    assert f["fill_sizes"][:, :2].tolist() == [[50, 25], [100, 25]]
+    assert b["last_prices"].tolist() == [40, 50]
+
+
+def test_oracle_last_price_persistence_scenario():
+    """market_tests.cu:753-811 (TestLastPricePersistence) with 128 price
+    levels: prices 200 and 210 are at or above max_price_levels and are not
+    added (market.cu:44, :73), so market 1 never fills and its last prices stay
+    0; market 0 fills at 100, then at 110.  Two BBOBatches are independent."""
+    m = oracle.OracleMarket(2, 128, 1024, 512, 16)
+    f = m.new_fill_batch()
+    b1, b2 = m.new_bbo_batch(), m.new_bbo_batch()
+    A = lambda *x: np.array(x, np.int32)  # noqa: E731
+    m.add_two_sided_quotes(A(100, 200), A(50, 100), A(100, 200), A(50, 100), A(0, 0), f)
+    m.update_last_prices(b1, f)
+    assert f["fill_counts"].tolist() == [1, 0]
+    assert b1["last_prices"].tolist() == [100, 0] and b2["last_prices"].tolist() == [0, 0]
+    m.add_two_sided_quotes(A(110, 210), A(25, 50), A(110, 210), A(25, 50), A(1, 1), f)
+    m.update_last_prices(b2, f)
+    assert b1["last_prices"].tolist() == [100, 0] and b2["last_prices"].tolist() == [110, 0]

@@ -227,3 +227,50 @@ def test_oracle_last_price_persistence_scenario():
     m.add_two_sided_quotes(A(110, 210), A(25, 50), A(110, 210), A(25, 50), A(1, 1), f)
     m.update_last_prices(b2, f)
     assert b1["last_prices"].tolist() == [100, 0] and b2["last_prices"].tolist() == [110, 0]
+
+
+def test_oracle_remaining_unit_scenarios():
+    """The other scenarios of market_tests.cu, answers derived by hand from
+    market.cu.  Same-price FIFO (:171-221): bids of 10, 20, 30 at 25 (tids 0,
+    2, 4) fill in time priority against an ask of 60 (tid 7), at 25 each.
+    Last-price tracking (:562-617): a new BBOBatch starts at 0 (market.cu:453;
+    the C++ test's NULL_INDEX is stale), one fill per market at the resting
+    bid's price, then only market 1 trades (the new bid rests, 65).
+    Several fills (:620-669): bids 60, 55, 50 are taken best first by an ask
+    of 300 at 50, so the last price is the third fill's, 50."""
+    A = lambda *x: np.array(x, np.int32)  # noqa: E731
+    m = oracle.OracleMarket(1, 128, 1024, 512, 16)
+    f = m.new_fill_batch()
+    for i in range(3):
+        m.add_two_sided_quotes(A(25), A(10 * (i + 1)), A(0), A(0), A(i), f)
+    m.add_two_sided_quotes(A(0), A(0), A(25), A(60), A(3), f)
+    assert int(f["fill_counts"][0]) == 3
+    assert f["fill_sizes"][0, :3].tolist() == [10, 20, 30]
+    assert f["fill_prices"][0, :3].tolist() == [25, 25, 25]
+    assert f["fill_quoter_ids"][0, :3].tolist() == [0, 1, 2]
+    assert f["fill_customer_ids"][0, :3].tolist() == [3, 3, 3]
+    assert f["fill_quote_tid"][0, :3].tolist() == [0, 2, 4] and f["fill_tid"][0, :3].tolist() == [7] * 3
+    assert not f["fill_is_sell_quote"][0, :3].any()
+
+    m = oracle.OracleMarket(3, 128, 1024, 512, 16)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    m.get_bbos(b)
+    assert b["last_prices"].tolist() == [0, 0, 0]
+    m.add_two_sided_quotes(A(50, 60, 70), A(100, 200, 300), A(50, 60, 70), A(50, 100, 150),
+                           A(0, 0, 0), f)
+    m.update_last_prices(b, f)
+    assert b["last_prices"].tolist() == [50, 60, 70]
+    m.add_two_sided_quotes(A(0, 65, 0), A(0, 50, 0), A(0, 65, 0), A(0, 25, 0), A(1, 1, 1), f)
+    m.update_last_prices(b, f)
+    assert f["fill_counts"].tolist() == [0, 1, 0]
+    assert b["last_prices"].tolist() == [50, 65, 70]
+
+    m = oracle.OracleMarket(1, 128, 1024, 512, 16)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    for i in range(3):
+        m.add_two_sided_quotes(A(50 + 5 * i), A(100), A(0), A(0), A(i), f)
+    m.add_two_sided_quotes(A(0), A(0), A(50), A(300), A(3), f)
+    m.update_last_prices(b, f)
+    assert int(f["fill_counts"][0]) == 3
+    assert f["fill_prices"][0, :3].tolist() == [60, 55, 50]
+    assert b["last_prices"].tolist() == [50]

@@ -209,3 +209,66 @@ def test_string_representation():
     s = market.to_string(0)
     for sub in ("sell orders", "buy orders", "px 50", "px 55", "sz 100", "sz 150"):
         assert sub in s
+
+
+def test_reference_unit_scenarios_on_gpu():
+    """The last-price and same-price FIFO scenarios of market_tests.cu
+    (:171-221, :562-811), answers derived by hand (tests/test_oracle_pins.py
+    states the derivations), through the CUDA path."""
+    # same-price FIFO
+    m = aom.VecMarket(1, 128, 1024, 512)
+    f = m.new_fill_batch()
+    for i in range(3):
+        m.add_two_sided_quotes(T(25), T(10 * (i + 1)), T(0), T(0), T(i), f)
+    m.add_two_sided_quotes(T(0), T(0), T(25), T(60), T(3), f)
+    assert f.fill_counts.tolist() == [3]
+    assert f.fill_sizes[0, :3].tolist() == [10, 20, 30]
+    assert f.fill_prices[0, :3].tolist() == [25, 25, 25]
+    assert f.fill_quoter_ids[0, :3].tolist() == [0, 1, 2]
+    assert f.fill_quote_tid[0, :3].tolist() == [0, 2, 4] and f.fill_tid[0, :3].tolist() == [7] * 3
+    # last-price tracking
+    m = aom.VecMarket(3, 128, 1024, 512)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    m.get_bbos(b)
+    assert b.last_prices.tolist() == [0, 0, 0]
+    m.add_two_sided_quotes(T([50, 60, 70]), T([100, 200, 300]), T([50, 60, 70]),
+                           T([50, 100, 150]), T([0, 0, 0]), f)
+    b.update_last_prices(f)
+    assert b.last_prices.tolist() == [50, 60, 70]
+    m.add_two_sided_quotes(T([0, 65, 0]), T([0, 50, 0]), T([0, 65, 0]), T([0, 25, 0]),
+                           T([1, 1, 1]), f)
+    b.update_last_prices(f)
+    assert b.last_prices.tolist() == [50, 65, 70]
+    # several fills
+    m = aom.VecMarket(1, 128, 1024, 512)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    for i in range(3):
+        m.add_two_sided_quotes(T(50 + 5 * i), T(100), T(0), T(0), T(i), f)
+    m.add_two_sided_quotes(T(0), T(0), T(50), T(300), T(3), f)
+    b.update_last_prices(f)
+    assert f.fill_prices[0, :3].tolist() == [60, 55, 50] and b.last_prices.tolist() == [50]
+    # reset and last price
+    m = aom.VecMarket(2, 128, 1024, 512)
+    f, b = m.new_fill_batch(), m.new_bbo_batch()
+    m.add_two_sided_quotes(T([45, 55]), T([100, 200]), T([45, 55]), T([100, 200]), T([0, 0]), f)
+    b.update_last_prices(f)
+    assert b.last_prices.tolist() == [45, 55]
+    m.reset()
+    m.add_two_sided_quotes(T([30, 40]), T([50, 100]), T([35, 45]), T([50, 100]), T([0, 0]), f)
+    b.update_last_prices(f)
+    assert f.fill_counts.tolist() == [0, 0] and b.last_prices.tolist() == [45, 55]
+    b.reset()
+    assert b.last_prices.tolist() == [0, 0]
+    m.add_two_sided_quotes(T([40, 50]), T([75, 125]), T([35, 45]), T([75, 125]), T([1, 1]), f)
+    b.update_last_prices(f)
+    assert f.fill_prices[:, :2].tolist() == [[35, 40], [45, 50]]
+    assert b.last_prices.tolist() == [40, 50]
+    # last price persistence across batches (200 and 210 are not below 128 levels)
+    m = aom.VecMarket(2, 128, 1024, 512)
+    f, b1, b2 = m.new_fill_batch(), m.new_bbo_batch(), m.new_bbo_batch()
+    m.add_two_sided_quotes(T([100, 200]), T([50, 100]), T([100, 200]), T([50, 100]), T([0, 0]), f)
+    b1.update_last_prices(f)
+    assert f.fill_counts.tolist() == [1, 0] and b1.last_prices.tolist() == [100, 0]
+    m.add_two_sided_quotes(T([110, 210]), T([25, 50]), T([110, 210]), T([25, 50]), T([1, 1]), f)
+    b2.update_last_prices(f)
+    assert b1.last_prices.tolist() == [100, 0] and b2.last_prices.tolist() == [110, 0]

@@ -274,3 +274,35 @@ def test_oracle_remaining_unit_scenarios():
     assert int(f["fill_counts"][0]) == 3
     assert f["fill_prices"][0, :3].tolist() == [60, 55, 50]
     assert b["last_prices"].tolist() == [50]
+
+
+@pytest.mark.parametrize("O,F", [(1, 4), (3, 2), (8, 16), (24, 512)])
+def test_reachable_state_invariants(O, F):
+    """The two facts the CUDA book does not store (it reads them from the
+    occupancy masks and the slot counter), checked on the reference
+    restatement over random steps with tight rings, ClearQuotes and Reset:
+    a level's head is -1 exactly when its tail is, and while the slot counter
+    is below O every record at or past it has no successor."""
+    N, L, C = 64, 16, 4
+    rng = np.random.default_rng(O * 100 + F)
+    m = oracle.OracleMarket(N, L, O, F, C)
+    f = m.new_fill_batch()
+    for t in range(300):
+        if t % 37 == 36:
+            m.reset()
+        elif t % 11 == 10:
+            m.clear_quotes(rng.random(N) < 0.4)
+        mid = rng.integers(4, 12, N)
+        m.add_two_sided_quotes((mid - rng.integers(-1, 3, N)).astype(np.int32),
+                               rng.integers(0, 5, N).astype(np.int32),
+                               (mid + rng.integers(-1, 3, N)).astype(np.int32),
+                               rng.integers(0, 5, N).astype(np.int32),
+                               rng.integers(0, C, N).astype(np.int32), f)
+        st = m.state()
+        for side in ("bid", "ask"):
+            h, tl = st[f"{side}_heads"], st[f"{side}_tails"]
+            assert np.array_equal(h == -1, tl == -1), (t, side)
+        cnt = st["order_next_slots"].astype(np.int64)
+        past = np.arange(O)[None, :] >= cnt[:, None]
+        live = (cnt < O)[:, None] & past
+        assert (st["order_next"][live] == -1).all(), t

@@ -91,5 +91,57 @@ def _compile(exe: str, verbose: bool) -> str:
     return LIB_PATH
 
 
+# ---- the C++ host side (cpp/vec_market.*): VecMarket for C++ callers ----
+
+CPP_DIR = os.path.join(ROOT_DIR, "cpp")
+CPP_LIB_PATH = os.path.join(LIB_DIR, "libastra_vec_market.so")
+
+
+def torch_paths():
+    """Include and library directories of the installed torch (C++ API, c10/cuda)."""
+    import torch
+    base = os.path.dirname(torch.__file__)
+    inc = [os.path.join(base, "include"), os.path.join(base, "include", "torch", "csrc", "api",
+                                                        "include"), "/usr/local/cuda/include"]
+    return inc, os.path.join(base, "lib")
+
+
+def build_cpp(verbose: bool = False) -> str:
+    """Compile the C++ host library (VecMarket, FillBatch, BBOBatch of market.h
+    over the C ABI) with g++, linked against the CUDA library and torch."""
+    lib = build()
+    srcs = [os.path.join(CPP_DIR, "vec_market.cpp"), os.path.join(CPP_DIR, "vec_market.h")]
+    stamp = CPP_LIB_PATH + ".digest"
+    h = hashlib.sha256()
+    for p in srcs + [os.path.join(INCLUDE_DIR, x) for x in HEADERS]:
+        with open(p, "rb") as f:
+            h.update(f.read())
+    digest = h.hexdigest()
+    if os.path.exists(CPP_LIB_PATH) and os.path.exists(stamp):
+        with open(stamp) as f:
+            if f.read().strip() == digest:
+                return CPP_LIB_PATH
+    inc, tlib = torch_paths()
+    tmp = CPP_LIB_PATH + f".tmp{os.getpid()}"
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", INCLUDE_DIR]
+    for d in inc:
+        cmd += ["-isystem", d]
+    cmd += [os.path.join(CPP_DIR, "vec_market.cpp"), "-o", tmp, "-L", LIB_DIR, "-lastra_market",
+            "-L", tlib, "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda",
+            f"-Wl,-rpath,{LIB_DIR}", f"-Wl,-rpath,{tlib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError("g++ failed building libastra_vec_market.so:\n" + res.stderr[-4000:])
+    os.replace(tmp, CPP_LIB_PATH)
+    with open(stamp, "w") as f:
+        f.write(digest)
+    del lib
+    return CPP_LIB_PATH
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True))
+    if "--cpp" in sys.argv:
+        print(build_cpp(verbose=True))

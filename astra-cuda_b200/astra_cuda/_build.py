@@ -126,9 +126,11 @@ def build_cpp(verbose: bool = False) -> str:
     cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", INCLUDE_DIR]
     for d in inc:
         cmd += ["-isystem", d]
+    # --no-as-needed keeps libtorch_cuda loaded: nothing references its symbols
+    # directly, but it registers torch's CUDA backend
     cmd += [os.path.join(CPP_DIR, "vec_market.cpp"), "-o", tmp, "-L", LIB_DIR, "-lastra_market",
-            "-L", tlib, "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda",
-            f"-Wl,-rpath,{LIB_DIR}", f"-Wl,-rpath,{tlib}"]
+            "-L", tlib, "-Wl,--no-as-needed", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10",
+            "-lc10_cuda", "-Wl,--as-needed", f"-Wl,-rpath,{LIB_DIR}", f"-Wl,-rpath,{tlib}"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)

@@ -107,10 +107,12 @@ def torch_paths():
 
 
 def build_cpp(verbose: bool = False) -> str:
-    """Compile the C++ host library (VecMarket, FillBatch, BBOBatch of market.h
-    over the C ABI) with g++, linked against the CUDA library and torch."""
+    """Compile the C++ host library (VecMarket, FillBatch, BBOBatch of market.h,
+    and the player-trading step, over the C ABI) with g++, linked against the
+    CUDA library and torch."""
     lib = build()
-    srcs = [os.path.join(CPP_DIR, "vec_market.cpp"), os.path.join(CPP_DIR, "vec_market.h")]
+    units = [os.path.join(CPP_DIR, f) for f in ("vec_market.cpp", "high_low_trading_step.cpp")]
+    srcs = units + [os.path.join(CPP_DIR, f) for f in ("vec_market.h", "high_low_trading_step.h")]
     stamp = CPP_LIB_PATH + ".digest"
     h = hashlib.sha256()
     for p in srcs + [os.path.join(INCLUDE_DIR, x) for x in HEADERS]:
@@ -123,12 +125,12 @@ def build_cpp(verbose: bool = False) -> str:
                 return CPP_LIB_PATH
     inc, tlib = torch_paths()
     tmp = CPP_LIB_PATH + f".tmp{os.getpid()}"
-    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", INCLUDE_DIR]
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", INCLUDE_DIR, "-I", CPP_DIR]
     for d in inc:
         cmd += ["-isystem", d]
     # --no-as-needed keeps libtorch_cuda loaded: nothing references its symbols
     # directly, but it registers torch's CUDA backend
-    cmd += [os.path.join(CPP_DIR, "vec_market.cpp"), "-o", tmp, "-L", LIB_DIR, "-lastra_market",
+    cmd += [*units, "-o", tmp, "-L", LIB_DIR, "-lastra_market",
             "-L", tlib, "-Wl,--no-as-needed", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10",
             "-lc10_cuda", "-Wl,--as-needed", f"-Wl,-rpath,{LIB_DIR}", f"-Wl,-rpath,{tlib}"]
     res = subprocess.run(cmd, capture_output=True, text=True)

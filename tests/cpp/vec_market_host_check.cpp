@@ -1,10 +1,12 @@
 // Host-side checks of the C++ VecMarket (astra-cuda_b200/cpp/vec_market.h)
 // that need no GPU: the constants of market.h:56-61 and the constructor's
-// argument checks (market.cu:338-350), which throw before any allocation.
+// argument checks (market.cu:338-350), which throw before any allocation; the
+// player-trading step's entry points (high_low_trading_step.h) must link.
 #include <iostream>
 #include <stdexcept>
 #include <string>
 
+#include "high_low_trading_step.h"
 #include "vec_market.h"
 
 using namespace astra::order_matching;
@@ -47,6 +49,11 @@ int main() {
   BBOBatch bb;
   (void)fb;
   (void)bb;
+  // the trading step's entry points resolve at link time
+  auto apply = &astra::high_low_trading::PlayerTradingStep::Apply;
+  auto observe = &astra::high_low_trading::PlayerTradingStep::FillObservation;
+  auto returns = &astra::high_low_trading::PlayerTradingStep::FillReturns;
+  if (!apply || !observe || !returns) ++failures;
   std::cout << (failures ? "FAILED" : "ok") << "\n";
   return failures;
 }

@@ -1,6 +1,7 @@
-"""The C++ host side (astra-cuda_b200/cpp/vec_market.*: market.h's FillBatch,
-BBOBatch and VecMarket over the C ABI) builds, links, and raises the
-reference's errors for bad constructor arguments; no GPU needed."""
+"""The C++ host side (astra-cuda_b200/cpp/: market.h's FillBatch, BBOBatch
+and VecMarket, and the player-trading step, over the C ABI) builds, links,
+and raises the reference's errors for bad constructor arguments; no GPU
+needed."""
 import os
 import subprocess
 

@@ -1,12 +1,14 @@
 // C ABI of the matching engine (include/astra_market.h) and of the fused
 // player-trading step (include/astra_trading.h): argument checks,
 // device guard, launches, error reporting.  No allocation happens here; all
-// buffers are the caller's.
+// buffers are the caller's, except the check-word scratch of the
+// allocation-free trading entry point, a static device array at the end.
 #include <cuda_runtime.h>
 
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "am_kernels.cuh"
@@ -571,6 +573,74 @@ int am_fill_observation(const am_market* mk, const am_trading_dims* td,
     am::observation_kernel<<<blocks, am::kBlock, 0, as_stream(stream)>>>(o);
   }
   return launch_status("FillObservationTensor");
+}
+
+}  // extern "C"
+
+// ---- allocation-free player-trading step (am_apply_player_trading_noalloc) ----
+//
+// The eight check words that am_check_player_moves writes and
+// am_apply_player_trading reads are scratch: the game never keeps them.  The
+// allocation-free entry point holds them in this file-scope device array
+// instead of a caller buffer, so a caller that cannot allocate device memory
+// passes only the game's inputs and outputs.  Every GPU that loads the library
+// holds the array until the process exits, and every call on that GPU shares
+// it.
+namespace {
+
+constexpr int kNoAllocScratchWords = 64;  // 256 bytes; one call uses words 0..7
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchWords];
+
+std::mutex g_noalloc_mu;
+uint32_t* g_noalloc_addr[kNoAllocMaxDevices];  // device address of the array, per GPU
+
+// Device address of g_noalloc_scratch on `device`, looked up once per device
+// with that device current (the caller's DeviceGuard has made it current).
+// In host code the array's name is only a host-side stand-in, never a device
+// address, so kernels are given this pointer instead.
+int noalloc_scratch(int device, uint32_t** out) {
+  if (device >= kNoAllocMaxDevices)
+    return fail(AM_ERR_INVALID, "device_id < %d for the allocation-free entry point (device_id = %d)",
+                kNoAllocMaxDevices, device);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(AM_ERR_CUDA, "cudaGetSymbolAddress of the check-word scratch on device %d: %s",
+                  device, cudaGetErrorString(e));
+    g_noalloc_addr[device] = static_cast<uint32_t*>(p);
+  }
+  *out = g_noalloc_addr[device];
+  return AM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int am_apply_player_trading_noalloc(const am_market* mk, const am_trading_dims* td,
+                                    const am_trading_state* st, const int32_t* moves,
+                                    int32_t trade_move_number, int32_t base_tid, int32_t* sticky,
+                                    int32_t* fills, int32_t* fill_counts, int32_t* bbos,
+                                    void* stream) {
+  int rc = check_trading(mk, td);
+  if (rc) return rc;
+  // one call needs eight scratch words whatever N, P and S are
+  static_assert(kNoAllocScratchWords >= 8, "the check words need 8 scratch words");
+  uint32_t* checks = nullptr;
+  {
+    DeviceGuard g(mk->device);
+    if (g.err) return fail(AM_ERR_CUDA, "cudaSetDevice(%d): %s", mk->device, cudaGetErrorString(g.err));
+    if ((rc = noalloc_scratch(mk->device, &checks))) return rc;
+  }
+  // am_check_player_moves sets the minima to ~0 and the maxima to 0 before it
+  // reduces, so nothing from the previous call survives into this one
+  if ((rc = am_check_player_moves(mk, moves, checks, stream))) return rc;
+  return am_apply_player_trading(mk, td, st, moves, trade_move_number, base_tid, checks, sticky,
+                                 fills, fill_counts, bbos, stream);
 }
 
 }  // extern "C"

@@ -87,6 +87,34 @@ int am_apply_player_trading(const am_market *mk, const am_trading_dims *td,
                             const uint32_t *checks, int32_t *sticky, int32_t *fills,
                             int32_t *fill_counts, int32_t *bbos, void *stream);
 
+/* Allocation-free ApplyPlayerTrading.  No counterpart in the reference: it is
+ * an addition for callers that cannot allocate device memory, such as a host
+ * framework that hands a plugin its input and output buffers and nothing
+ * else, or a process that runs under a fixed device-memory budget where a
+ * cudaMalloc mid-rollout would fail or stall every stream while the device
+ * synchronises.  It is am_check_player_moves followed by
+ * am_apply_player_trading with deferred checks, the same two launches, but
+ * the eight check words live in a 256-byte static device array inside the
+ * library (held by every GPU that loads it until the process exits) instead
+ * of a caller buffer.  The caller passes only the game's inputs and outputs:
+ * sticky (nullable, int32 [9]) records the first failing check as
+ * am_apply_player_trading does.  The scratch needs 8 words for any N, P and S,
+ * so no size can exceed it; every other limit is the two calls' own.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - The check words are re-initialised by every call (minima to ~0, maxima
+ *    to 0) before the reduction, so one call's values never reach the next.
+ *  - Every call on a device shares the array: calls that can overlap on the
+ *    GPU (different streams, no ordering between them) race on it.  Issue
+ *    them on one stream, or use the allocating pair above.
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+int am_apply_player_trading_noalloc(const am_market *mk, const am_trading_dims *td,
+                                    const am_trading_state *st, const int32_t *moves,
+                                    int32_t trade_move_number, int32_t base_tid,
+                                    int32_t *sticky, int32_t *fills, int32_t *fill_counts,
+                                    int32_t *bbos, void *stream);
+
 /* FillReturns (high_low_trading.cc:345-371) into returns = int32 [N][P]:
  * cash + contracts * settlement value - (target != 0) * |contracts - target| * V. */
 int am_fill_returns(const am_market *mk, const am_trading_dims *td,

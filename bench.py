@@ -24,6 +24,9 @@ Also reported on the same line:
   over markets) timed on a sample of the same workload, rank 0, N = 1 only;
 * ``unfused`` -- the same steps with GetBBOs as its own launch, the call
   pattern of the reference's API;
+* ``reference_gpu`` (N = 1) -- B0: the reference's own engine (market.cu
+  compiled unchanged for sm_100a, oracle/_ref/) on the same GPU, quotes and
+  step window, timed the same way; its last step must equal this engine's;
 * ``gather`` (N > 1) -- NCCL gather of BBOs and positions to rank 0, timed
   separately from matching.
 
@@ -67,6 +70,8 @@ def parse():
                     help="run only the fused trading legs (for profiling)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip unfused/e2e/replay legs")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the B0 leg (the reference's engine built for this GPU)")
     ap.add_argument("--snapshot", default="",
                     help="file holding the book after the pre-roll: written when absent, "
                          "loaded (no pre-roll launches) when present; for small profiling runs")
@@ -137,13 +142,40 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def workloads_without_library():
+    """``astra_cuda/workloads.py`` loaded by file path, outside the package:
+    the configuration table and the bytes model without the package's
+    ``__init__``, which loads this repository's CUDA library.  The reference
+    arm uses it so that nothing of this repository's engine is mapped into
+    that process."""
+    import importlib.util
+    path = os.path.join(ROOT, "astra-cuda_b200", "astra_cuda", "workloads.py")
+    spec = importlib.util.spec_from_file_location("_bench_workload_table", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def mapped_repo_libraries():
+    """This repository's own CUDA/C++ libraries mapped into the process."""
+    names = ("libastra_market.so", "libastra_vec_market.so")
+    try:
+        with open("/proc/self/maps") as f:
+            return sorted({ln.split()[-1] for ln in f if ln.rstrip().endswith(names)})
+    except OSError:
+        return []
+
+
 def run_reference(args, rank):
     """--impl reference: the CPU restatement of market.cu on host threads."""
     if rank != 0:
         return
-    from astra_cuda import workloads
+    workloads = workloads_without_library()
     cfg = workloads.CONFIGS[args.config]
     res = cpu_baseline(cfg, args, sample=args.cpu_sample)
+    leaked = mapped_repo_libraries()
+    if leaked:
+        raise RuntimeError(f"the reference arm mapped this repository's libraries: {leaked}")
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["ms_per_step"], "p50_step_ms": res["p50_step_ms"],
@@ -377,6 +409,64 @@ def trading_leg(dev, envs, fused_only=False):
     return out
 
 
+def reference_gpu_leg(cfg, N, pre, qs, W, K, dev, our_counts, our_bbos):
+    """B0: the reference's own engine (market.cu compiled unchanged for
+    sm_100a, oracle/_ref/libref_market.so) on this GPU, with its own call
+    pattern -- AddTwoSidedQuotes then GetBBOs, each its own launches
+    (fill_counts.zero_, add_orders_kernel, match_orders_kernel,
+    get_bbo_kernel) -- over the same quote stream and step window as the timed
+    run: an untimed pre-roll of `pre` steps, W warm-up steps and K timed steps
+    with per-step CUDA events.  Its fill counts and BBOs after the last step
+    must equal this engine's."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref_gpu
+    from astra_cuda import workloads
+    if not ref_gpu.available():
+        return {"unavailable": "oracle/_ref/libref_market.so not built"}
+    L, O, F, C = cfg["L"], cfg["O"], cfg["F"], cfg["C"]
+    ref = ref_gpu.RefVecMarket(N, L, O, F, C, device_id=dev.index)
+    stream = workloads.DeviceQuoteStream(cfg["gen"], 0, N, dev)
+    cur = torch.cuda.current_stream(dev)
+    with ref_gpu.quiet():
+        t = 0
+        while t < pre:
+            k = min(64, pre - t)
+            q = stream.take(k)
+            for i in range(k):
+                ref.add_two_sided_quotes(*q[i])
+                ref.get_bbos()
+            t += k
+        del q
+        for i in range(W):
+            ref.add_two_sided_quotes(*qs[i])
+            ref.get_bbos()
+        torch.cuda.synchronize()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+        evs[0].record(cur)
+        for i in range(K):
+            ref.add_two_sided_quotes(*qs[W + i])
+            ref.get_bbos()
+            evs[i + 1].record(cur)
+        torch.cuda.synchronize()
+    step_ms = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(K))
+    total = evs[0].elapsed_time(evs[K])
+    same = bool(torch.equal(ref.view("fill_counts"), our_counts)) and \
+        bool(torch.equal(ref.bbos()[:4], our_bbos))
+    out = {"ms_per_step": total / K, "value": N * K / (total * 1e-3), "unit": UNIT,
+           "p50_step_ms": step_ms[len(step_ms) // 2],
+           "p99_step_ms": step_ms[min(len(step_ms) - 1, int(0.99 * len(step_ms)))],
+           "threads_per_block": 64, "launches_per_step": 4,
+           "bit_exact_last_step": same,
+           "what": "the reference's VecMarket (market.cu unchanged, sm_100a, -O3 -DNDEBUG) "
+                   "on this GPU: AddTwoSidedQuotes + GetBBOs per step, CUDA events, same "
+                   "quotes and step window as the timed run; device printf of the "
+                   "fill-overflow path sent to /dev/null"}
+    del ref
+    torch.cuda.empty_cache()
+    return out
+
+
 def config_dict(cfg, args, markets, world):
     return {"workload": f"config{args.config}:{cfg['name']}", "markets_per_gpu": markets,
             "total_markets": markets * world, "max_price_levels": cfg["L"],
@@ -468,6 +558,7 @@ def main():
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(K)]
     total_ms = evs[0].elapsed_time(evs[K])
     last_counts = fills.fill_counts.clone()
+    last_bbos = bbos.storage[:4].clone()
 
     extras = {}
     if snap is not None:
@@ -506,6 +597,17 @@ def main():
         extras["events"] = dict(zip(("n_ins", "n_fill", "n_rm", "n_empty", "n_touch"), e))
         del snap, rfills, rkw
         torch.cuda.empty_cache()
+
+    # B0: the reference's engine on this GPU, same quotes and step window
+    if not args.no_extras and not args.no_reference_gpu and world == 1:
+        try:
+            extras["reference_gpu"] = reference_gpu_leg(cfg, N, pre, qs, W, K, dev, last_counts,
+                                                        last_bbos)
+            rg = extras["reference_gpu"]
+            if "ms_per_step" in rg:
+                rg["speedup"] = round(rg["ms_per_step"] / (total_ms / K), 2)
+        except Exception as ex:  # reported, never fatal for the GPU number
+            extras["reference_gpu"] = {"error": repr(ex)}
 
     # e2e: quotes from pinned host memory every step, fill counts back
     e2e = None

@@ -7,6 +7,7 @@
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace astra {
 namespace high_low_trading {
@@ -21,6 +22,15 @@ void Check(int rc, const char* what) {
 }
 
 int32_t* I32(const torch::Tensor& t) { return t.data_ptr<int32_t>(); }
+
+// ASTRA_CHECK_OP's message (astra_utils.h:116-124)
+template <typename A, typename B>
+void CheckOp(bool ok, const char* xs, const char* op, const char* ys, A x, B y) {
+  if (ok) return;
+  std::ostringstream s;
+  s << xs << " " << op << " " << ys << "\n" << xs << " = " << x << ", " << ys << " = " << y;
+  Fatal(s.str());
+}
 
 void* Stream(int device) { return c10::cuda::getCurrentCUDAStream(device).stream(); }
 
@@ -64,7 +74,60 @@ std::string FirstFailure(const int32_t* words, int32_t V, int32_t T) {
   return "";
 }
 
+void CheckField(const torch::Tensor& t, const char* name, std::vector<int64_t> shape,
+                torch::ScalarType dtype, const torch::Device& device, bool any_strides) {
+  bool ok = t.defined() && t.dim() == (int64_t)shape.size() && t.scalar_type() == dtype &&
+            t.device() == device;
+  for (size_t k = 0; ok && k < shape.size(); ++k) ok = t.size((int64_t)k) == shape[k];
+  if (ok && any_strides) {
+    for (int64_t k = 0; k < t.dim(); ++k) ok = ok && t.stride(k) >= 1;
+  } else if (ok) {
+    ok = t.is_contiguous();
+  }
+  if (ok) return;
+  std::ostringstream s;
+  s << name << " must be a" << (dtype == torch::kBool ? " bool" : "n int32") << " tensor of shape [";
+  for (size_t k = 0; k < shape.size(); ++k) s << (k ? ", " : "") << shape[k];
+  s << "] on device " << device.str() << (any_strides ? " with positive strides" : ", contiguous");
+  Fatal(s.str());
+}
+
 }  // namespace
+
+void CheckTradingTensors(const TradingTensors& st, int64_t num_envs, int32_t players,
+                         int32_t steps_per_player, const torch::Device& device, unsigned fields) {
+  const int64_t N = num_envs, P = players, S = steps_per_player;
+  const auto I = torch::kInt32;
+  // read by all three calls
+  CheckField(st.contract_values, "contract_values", {N, 3}, I, device, false);
+  CheckField(st.target_positions, "target_positions", {N, P}, I, device, false);
+  if (fields & (kTradingApply | kTradingObservation))
+    CheckField(st.player_contract_over_time, "player_contract_over_time", {N, P, S, 6}, I,
+               device, true);
+  if (fields & kTradingApply) {
+    CheckField(st.player_last_positions, "player_last_positions", {N, P, 2}, I, device, false);
+    CheckField(st.market_contract_over_time, "market_contract_over_time", {N, P * S, 3}, I,
+               device, true);
+    CheckField(st.immediate_rewards, "immediate_rewards", {N, P}, I, device, false);
+    CheckField(st.rewards_since_last_action, "rewards_since_last_action", {N, P}, I, device,
+               false);
+  }
+  if (fields & kTradingObservation) {
+    CheckField(st.player_permutation, "player_permutation", {N, P}, I, device, false);
+    CheckField(st.contract_high_settle, "contract_high_settle", {N}, torch::kBool, device, false);
+  }
+}
+
+void CheckReturnsBuffer(const torch::Tensor& returns, int64_t num_envs, int32_t players,
+                        const torch::Device& device) {
+  // high_low_trading.cc:347-349
+  CheckOp(returns.dim() == 2, "returns_buffer.dim()", "==", "2", returns.dim(), 2);
+  CheckOp(returns.size(0) == num_envs, "returns_buffer.size(0)", "==", "num_envs_",
+          returns.size(0), num_envs);
+  CheckOp(returns.size(1) == players, "returns_buffer.size(1)", "==", "num_players_",
+          returns.size(1), players);
+  if (returns.device() != device) Fatal("returns_buffer must be on device " + device.str());
+}
 
 PlayerTradingStep::PlayerTradingStep(const order_matching::VecMarket& market, int32_t players,
                                      int32_t steps_per_player, int32_t max_contract_value,
@@ -81,9 +144,16 @@ void PlayerTradingStep::Apply(order_matching::VecMarket& market, order_matching:
                               torch::Tensor move, int32_t trade_move_number) {
   const am_market* mk = market.abi();
   const int dev = mk->device;
+  const torch::Device device(torch::kCUDA, dev);
   if (move.dim() != 2 || move.size(0) != mk->dims.num_markets || move.size(1) != 4)
     Fatal("move must be an int32 [num_envs, 4] tensor (bid_px, ask_px, bid_sz, ask_sz)");
   if (move.scalar_type() != torch::kInt32) Fatal("expected scalar type Int for move");
+  if (move.device() != device) Fatal("move tensor must be on device " + device.str());
+  CheckTradingTensors(st, mk->dims.num_markets, td_.num_players, td_.steps_per_player, device,
+                      kTradingApply);
+  order_matching::CheckFillBatch(fills, mk->dims.num_markets,
+                                 mk->dims.max_active_fills_per_market, device);
+  order_matching::CheckBBOBatch(bbos, mk->dims.num_markets, device);
   move = move.contiguous();
   if (reinterpret_cast<uintptr_t>(move.data_ptr()) % 16 != 0) move = move.clone();
   void* stream = Stream(dev);
@@ -111,9 +181,14 @@ void PlayerTradingStep::FillObservation(const order_matching::VecMarket& market,
                                         int32_t trade_move_number, torch::Tensor values) const {
   const am_market* mk = market.abi();
   const int32_t P = td_.num_players, S = td_.steps_per_player;
+  const torch::Device device(torch::kCUDA, mk->device);
   if (values.scalar_type() != torch::kFloat32 || !values.is_contiguous() || values.dim() != 2 ||
-      values.size(0) != mk->dims.num_markets || values.size(1) != 12 + 6 * P)
-    Fatal("values must be a contiguous float32 [num_envs, 12 + 6 * players] tensor");
+      values.size(0) != mk->dims.num_markets || values.size(1) != 12 + 6 * P ||
+      values.device() != device)
+    Fatal("values must be a contiguous float32 [num_envs, 12 + 6 * players] tensor on device " +
+          device.str());
+  CheckTradingTensors(st, mk->dims.num_markets, P, S, device, kTradingObservation);
+  order_matching::CheckBBOBatch(bbos, mk->dims.num_markets, device);
   const auto& pc = st.player_contract_over_time;
   am_observation_inputs in{I32(st.player_permutation), I32(st.contract_values),
                            reinterpret_cast<const uint8_t*>(st.contract_high_settle.data_ptr<bool>()),
@@ -131,11 +206,20 @@ void PlayerTradingStep::FillObservation(const order_matching::VecMarket& market,
 void PlayerTradingStep::FillReturns(const order_matching::VecMarket& market,
                                     const TradingTensors& st, torch::Tensor returns) const {
   const am_market* mk = market.abi();
-  if (returns.scalar_type() != torch::kInt32 || !returns.is_contiguous())
-    Fatal("returns must be a contiguous int32 [num_envs, players] tensor");
-  Check(am_fill_returns(mk, &td_, I32(st.contract_values), I32(st.target_positions), I32(returns),
+  const int32_t N = mk->dims.num_markets, P = td_.num_players;
+  const torch::Device device(torch::kCUDA, mk->device);
+  CheckReturnsBuffer(returns, N, P, device);
+  CheckTradingTensors(st, N, P, td_.steps_per_player, device, kTradingReturns);
+  // the kernel writes int32 rows; other dtypes or layouts receive a copy, as
+  // the reference's torch ops would write them
+  const bool direct = returns.scalar_type() == torch::kInt32 && returns.is_contiguous();
+  torch::Tensor out = direct ? returns
+                             : torch::empty({N, P}, torch::TensorOptions().device(device)
+                                                        .dtype(torch::kInt32));
+  Check(am_fill_returns(mk, &td_, I32(st.contract_values), I32(st.target_positions), I32(out),
                         Stream(mk->device)),
         "FillReturns");
+  if (!direct) returns.copy_(out);
 }
 
 }  // namespace high_low_trading

@@ -29,6 +29,23 @@ struct TradingTensors {
   torch::Tensor rewards_since_last_action;  // [N, P]
 };
 
+// Argument checks run before any launch, by the shapes the reference gives
+// its tensors (high_low_trading.cc:80-92): every field int32 on `device` (the
+// market's) with its reference shape, contiguous except the two history
+// tensors, which may have any positive strides; contract_high_settle is bool.
+// `fields` selects what a call reads or writes (the kTrading* bits below).
+// Exposed so host-side tests can run them without a GPU.
+enum : unsigned {
+  kTradingApply = 1u,        // ApplyPlayerTrading's tensors
+  kTradingObservation = 2u,  // FillObservationTensor's tensors
+  kTradingReturns = 4u,      // FillReturns' tensors
+};
+void CheckTradingTensors(const TradingTensors& st, int64_t num_envs, int32_t players,
+                         int32_t steps_per_player, const torch::Device& device, unsigned fields);
+// FillReturns' buffer checks (high_low_trading.cc:347-349) plus its device.
+void CheckReturnsBuffer(const torch::Tensor& returns, int64_t num_envs, int32_t players,
+                        const torch::Device& device);
+
 class PlayerTradingStep {
  public:
   // Checks the market against the game's sizes (am_trading_validate) and
@@ -46,12 +63,14 @@ class PlayerTradingStep {
              order_matching::BBOBatch& bbos, TradingTensors& st, torch::Tensor move,
              int32_t trade_move_number);
 
-  // FillObservationTensor (:510-601) into values (float32 [N, 12 + 6P]).
+  // FillObservationTensor (:510-601) into values (contiguous float32
+  // [N, 12 + 6P] on the market's device).
   void FillObservation(const order_matching::VecMarket& market, const order_matching::BBOBatch& bbos,
                        const TradingTensors& st, int32_t player, int32_t trade_move_number,
                        torch::Tensor values) const;
 
-  // FillReturns (:345-371) into returns (int32 [N, P]).
+  // FillReturns (:345-371) into returns ([N, P] on the market's device; an
+  // int32 contiguous buffer is written directly, any other receives a copy).
   void FillReturns(const order_matching::VecMarket& market, const TradingTensors& st,
                    torch::Tensor returns) const;
 

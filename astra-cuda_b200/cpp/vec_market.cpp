@@ -36,7 +36,45 @@ int32_t* I32m(const torch::Tensor& t) { return t.data_ptr<int32_t>(); }
 
 constexpr int kSellByte = 28;  // is_sell_quote: low byte of record word 7
 
+std::string DeviceName(const torch::Device& d) { return d.str(); }
+
 }  // namespace
+
+void CheckQuoteTensor(const torch::Tensor& t, const char* name, int64_t num_markets,
+                      const torch::Device& device) {
+  if (!t.defined()) Fatal(std::string(name) + " tensor is undefined");
+  CheckOp(t.dim() == 1, (std::string(name) + ".dim()").c_str(), "==", "1", t.dim(), 1);
+  CheckOp(t.size(0) == num_markets, (std::string(name) + ".size(0)").c_str(), "==",
+          "num_markets_", t.size(0), num_markets);
+  if (t.device() != device)  // market.cu:474-504
+    Fatal(std::string(name) + " tensor must be on device " + DeviceName(device));
+  if (!t.is_contiguous()) Fatal(std::string(name) + " tensor must be contiguous");
+  if (t.scalar_type() != torch::kInt32)
+    Fatal(std::string("expected scalar type Int for ") + name);
+}
+
+void CheckFillBatch(const FillBatch& fills, int64_t num_markets, int64_t max_fills,
+                    const torch::Device& device) {
+  const torch::Tensor& r = fills.fill_records;
+  const torch::Tensor& c = fills.fill_counts;
+  if (!r.defined() || r.dim() != 3 || r.size(0) != num_markets || r.size(1) != max_fills ||
+      r.size(2) != AM_FILL_WORDS || r.scalar_type() != torch::kInt32 || !r.is_contiguous() ||
+      r.device() != device)
+    Fatal("fills.fill_records must be a contiguous int32 [num_markets, max_active_fills, 8] "
+          "tensor on " + DeviceName(device) + " (a FillBatch from NewFillBatch())");
+  if (!c.defined() || c.dim() != 1 || c.size(0) != num_markets ||
+      c.scalar_type() != torch::kInt32 || !c.is_contiguous() || c.device() != device)
+    Fatal("fills.fill_counts must be a contiguous int32 [num_markets] tensor on " +
+          DeviceName(device));
+}
+
+void CheckBBOBatch(const BBOBatch& bbos, int64_t num_markets, const torch::Device& device) {
+  const torch::Tensor& s = bbos.storage;
+  if (!s.defined() || s.dim() != 2 || s.size(0) != 5 || s.size(1) != num_markets ||
+      s.scalar_type() != torch::kInt32 || !s.is_contiguous() || s.device() != device)
+    Fatal("bbos.storage must be a contiguous int32 [5, num_markets] tensor on " +
+          DeviceName(device) + " (a BBOBatch from NewBBOBatch())");
+}
 
 // ---- FillBatch (market.h:64-92, market.cu:420-439, 758-760) ----
 
@@ -101,7 +139,11 @@ BBOBatch& BBOBatch::operator=(const BBOBatch& other) {
 void BBOBatch::Reset() { storage.zero_(); }
 
 void BBOBatch::UpdateLastPrices(FillBatch& fills) {
+  if (!storage.defined()) Fatal("UpdateLastPrices on an empty BBOBatch");
   const int64_t n = storage.size(1);
+  CheckBBOBatch(*this, n, storage.device());
+  CheckFillBatch(fills, n, fills.fill_records.defined() ? fills.fill_records.size(1) : 0,
+                 storage.device());
   CheckOp(fills.fill_counts.size(0) == n, "fills.fill_counts.size(0)", "==",
           "last_prices.size(0)", fills.fill_counts.size(0), n);
   CheckOp(fills.fill_counts.device() == storage.device(), "fills.fill_counts.device()", "==",
@@ -198,19 +240,8 @@ void VecMarket::AddTwoSidedQuotes(torch::Tensor bid_px, torch::Tensor bid_sz, to
   const char* names[5] = {"bid_px", "bid_sz", "ask_px", "ask_sz", "customer_ids"};
   torch::Tensor* ts[5] = {&bid_px, &bid_sz, &ask_px, &ask_sz, &customer_ids};
   const torch::Device dev(torch::kCUDA, device_id_);
-  for (int i = 0; i < 5; ++i) {  // market.cu:467-504
-    CheckOp(ts[i]->size(0) == num_markets_, names[i], "==", "num_markets_", ts[i]->size(0),
-            num_markets_);
-    if (ts[i]->device() != dev)
-      Fatal(std::string(names[i]) + " tensor must be on device " + std::to_string(device_id_));
-    if (!ts[i]->is_contiguous()) Fatal(std::string(names[i]) + " tensor must be contiguous");
-    if (ts[i]->scalar_type() != torch::kInt32)
-      Fatal(std::string("expected scalar type Int for ") + names[i]);
-  }
-  if (!fills.fill_records.defined() || fills.fill_records.size(0) != num_markets_ ||
-      fills.fill_records.size(1) != max_fills_per_market_ || fills.fill_records.device() != dev)
-    Fatal("fills must come from NewFillBatch() of a market with the same num_markets, "
-          "max_active_fills_per_market and device");
+  for (int i = 0; i < 5; ++i) CheckQuoteTensor(*ts[i], names[i], num_markets_, dev);
+  CheckFillBatch(fills, num_markets_, max_fills_per_market_, dev);
   int32_t* rec = fills.fill_records.numel() ? I32m(fills.fill_records) : nullptr;
   Check(am_add_two_sided_quotes(&mk_, I32(bid_px), I32(bid_sz), I32(ask_px), I32(ask_sz),
                                 I32(customer_ids), global_tid_counter_, rec,
@@ -221,9 +252,7 @@ void VecMarket::AddTwoSidedQuotes(torch::Tensor bid_px, torch::Tensor bid_sz, to
 }
 
 void VecMarket::GetBBOs(BBOBatch& bbos) {
-  if (!bbos.storage.defined() || bbos.storage.size(1) != num_markets_ ||
-      bbos.storage.device() != torch::Device(torch::kCUDA, device_id_))
-    Fatal("bbos must be a BBOBatch of this market's size and device");
+  CheckBBOBatch(bbos, num_markets_, torch::Device(torch::kCUDA, device_id_));
   Check(am_get_bbos(&mk_, I32m(bbos.best_bid_prices), I32m(bbos.best_bid_sizes),
                     I32m(bbos.best_ask_prices), I32m(bbos.best_ask_sizes), Stream()),
         "GetBBOs");

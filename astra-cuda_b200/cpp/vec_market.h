@@ -89,6 +89,18 @@ class BBOBatch {
   void Bind();
 };
 
+// Argument checks on the caller-owned output batches, run by VecMarket before
+// any kernel writes them (the kernels write N*F records, N counts and 5*N BBO
+// words at the buffers' addresses, so a smaller, strided or wrongly typed
+// buffer would be written out of bounds).  `device` is the market's device.
+// Exposed so host-side tests can run them without a GPU.
+void CheckFillBatch(const FillBatch& fills, int64_t num_markets, int64_t max_fills,
+                    const torch::Device& device);
+void CheckBBOBatch(const BBOBatch& bbos, int64_t num_markets, const torch::Device& device);
+// One quote tensor of AddTwoSidedQuotes (market.cu:467-504, plus 1-D and int32).
+void CheckQuoteTensor(const torch::Tensor& t, const char* name, int64_t num_markets,
+                      const torch::Device& device);
+
 // market.h:121-350
 class VecMarket {
  public:

@@ -101,14 +101,6 @@ FillBatch::FillBatch(const FillBatch& other)
   if (fill_records.defined()) Bind();
 }
 
-FillBatch& FillBatch::operator=(const FillBatch& other) {
-  if (this != &other) {
-    FillBatch copy(other);
-    *this = std::move(copy);
-  }
-  return *this;
-}
-
 void FillBatch::Reset() { fill_counts.zero_(); }
 
 // ---- BBOBatch (market.h:95-119, market.cu:441-456, 788-825) ----
@@ -126,14 +118,6 @@ void BBOBatch::Bind() {
 BBOBatch::BBOBatch(const BBOBatch& other)
     : storage(other.storage.defined() ? other.storage.clone() : torch::Tensor()) {
   if (storage.defined()) Bind();
-}
-
-BBOBatch& BBOBatch::operator=(const BBOBatch& other) {
-  if (this != &other) {
-    BBOBatch copy(other);
-    *this = std::move(copy);
-  }
-  return *this;
 }
 
 void BBOBatch::Reset() { storage.zero_(); }

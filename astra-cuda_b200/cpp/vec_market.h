@@ -56,7 +56,9 @@ class FillBatch {
 
   FillBatch() = default;
   FillBatch(const FillBatch& other);  // deep copy (market.h:80-89)
-  FillBatch& operator=(const FillBatch& other);
+  // Assignment shares the other batch's tensors, as the reference's
+  // implicitly declared assignment does (e.g. fill_batch_ = NewFillBatch()).
+  FillBatch& operator=(const FillBatch& other) = default;
 
   void Reset();  // market.cu:758-760
 
@@ -78,7 +80,8 @@ class BBOBatch {
 
   BBOBatch() = default;
   BBOBatch(const BBOBatch& other);  // deep copy (market.h:107-112)
-  BBOBatch& operator=(const BBOBatch& other);
+  // Assignment shares the other batch's tensors, like the reference's.
+  BBOBatch& operator=(const BBOBatch& other) = default;
 
   void Reset();                             // market.cu:788-796
   void UpdateLastPrices(FillBatch& fills);  // market.cu:798-825

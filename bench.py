@@ -70,6 +70,8 @@ def parse():
                     help="run only the fused trading legs (for profiling)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip unfused/e2e/replay legs")
+    ap.add_argument("--sector-probe", action="store_true",
+                    help="measure scattered-sector access rates of this GPU and exit")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip the B0 leg (the reference's engine built for this GPU)")
     ap.add_argument("--snapshot", default="",
@@ -477,9 +479,52 @@ def config_dict(cfg, args, markets, world):
                   "and reads fresh quotes"}
 
 
+def sector_probe():
+    """--sector-probe: scattered 32-byte-sector access rates of this GPU
+    (astra-cuda_b200/measure/random_sector_probe.cu): dependent loads,
+    independent stores, load+store pairs and reductions, each uniformly spread
+    over 4 GB, at 4 and 8 resident 256-thread blocks per SM.  The step kernel
+    is made of exactly these accesses; the rates bound what it can reach."""
+    import torch
+    src = os.path.join(ROOT, "astra-cuda_b200", "measure", "random_sector_probe.cu")
+    out_dir = os.path.join(ROOT, "astra-cuda_b200", "measure", "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    so = os.path.join(out_dir, "librandom_sector_probe.so")
+    if not os.path.exists(so) or os.path.getmtime(so) < os.path.getmtime(src):
+        subprocess.run(["nvcc", "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+                        "-Xcompiler", "-fPIC", "-shared", "-o", so, src], check=True)
+    torch.cuda.init()
+    lib = ctypes.CDLL(so)
+    lib.probe_run.restype = ctypes.c_float
+    lib.probe_run.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
+                              ctypes.c_int]
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    res = {"what": "scattered 4-byte accesses, one per 32-byte sector, uniform over 4 GB "
+                   "(far above L2), per-thread chains; accesses/s of the whole grid "
+                   "(median of 5 launches, CUDA events); sector_GB_s = accesses/s x 32 B",
+           "sms": sms, "rates": []}
+    steps = 64
+    for mode, name in enumerate(("dependent_load", "store", "load_then_store", "reduction")):
+        for per_sm in (4, 8):
+            blocks = sms * per_sm
+            ms = lib.probe_run(mode, 4 << 30, blocks, steps, 5)
+            if ms <= 0:
+                res["rates"].append({"mode": name, "error": float(ms)})
+                continue
+            acc = blocks * 256 * steps / (ms * 1e-3)
+            res["rates"].append({"mode": name, "threads_per_sm": per_sm * 256,
+                                 "G_accesses_per_s": round(acc / 1e9, 2),
+                                 "sector_GB_s": round(acc * 32 / 1e9, 1), "ms": round(ms, 4)})
+    peak, src_peak = measured_peak()
+    res["copy_bandwidth_GB_s"] = peak
+    print(json.dumps({"sector_probe": res}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.sector_probe:
+        return sector_probe()
     if args.impl == "reference":
         return run_reference(args, rank)
     if args.trading_only:  # the fused trading legs alone (small profiling runs)

@@ -28,8 +28,9 @@ CONFIGS = {
             gen=dict(_GEN_WALK1), bbo_every_step=True, pos64=False),
     2: dict(name="scale_sweep", markets=[100_000, 300_000, 1_000_000], L=128, O=1024, F=1024,
             C=16, steps=500, gen=dict(_GEN_WALK1, walk=2), bbo_every_step=True, pos64=False),
-    # BASELINE gives no step count, absence rate or customer rotation for this
-    # shape: 2000 steps (so the 1024-slot ring wraps), p = 0.1 and step % 64.
+    # The contention shape's benchmark statement gives no step count, absence
+    # rate or customer rotation: 2000 steps (so the 1024-slot ring wraps),
+    # p = 0.1 and step % 64 are this repository's choices.
     3: dict(name="contention_100k", markets=[100_000], L=128, O=1024, F=1024, C=64, steps=2000,
             gen=dict(seed=0, kind=1, walk=0, mid_lo=64, mid_hi=64, cid_cycle=64),
             bbo_every_step=True, pos64=False),

@@ -13,8 +13,12 @@
 //                                ask head slot, its size, as the last step left
 //                                them; slot -1 = unknown.  Derived state: it
 //                                saves loads and makes GetBBOs coalesced.
-//   orders  int4   [N][O]        order record {size, customer id, tid,
+//   orders  int4   [N][O][2]     order record {size, customer id, tid,
 //                                next:int16 | price:uint8<<16 | is_bid<<24}
+//                                in the first 16 bytes of a 32-byte slot; the
+//                                second half is padding, so that an insert
+//                                writes its whole 32-byte sector and L2 never
+//                                has to fetch that sector's old contents
 //
 // Every access a step makes to a level or an order is a single 4- or 16-byte
 // access inside one 32-byte sector, so each costs one sector of DRAM traffic.
@@ -37,6 +41,7 @@ namespace am {
 
 constexpr uint32_t kEmptyLevel = 0xFFFFFFFFu;  // head = tail = -1
 constexpr int kBlock = 256;
+constexpr int kRecInt4 = 2;  // int4 units per order slot (32 bytes)
 
 struct Layout {
   size_t off_slots, off_mask, off_levels, off_bbo, off_orders, total;
@@ -51,7 +56,7 @@ __host__ __device__ inline Layout layout_of(int64_t N, int64_t L, int64_t O) {
   l.off_mask = o;   o = align256(o + 32 * (size_t)N);
   l.off_levels = o; o = align256(o + 8 * (size_t)N * (size_t)L);
   l.off_bbo = o;    o = align256(o + 16 * (size_t)N);  // after the levels: both start at 0xFF
-  l.off_orders = o; o = align256(o + 16 * (size_t)N * (size_t)O);
+  l.off_orders = o; o = align256(o + 16 * kRecInt4 * (size_t)N * (size_t)O);
   l.total = o;
   return l;
 }
@@ -156,9 +161,16 @@ __device__ __forceinline__ int ld_rec_size(const int4* p) {
   asm volatile("ld.global.s32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
   return r;
 }
+// The record of `slot` in a market's order array.
+__device__ __forceinline__ int4* rec_at(int4* rec, int slot) { return rec + kRecInt4 * slot; }
+__device__ __forceinline__ const int4* rec_at(const int4* rec, int slot) {
+  return rec + kRecInt4 * slot;
+}
+// A whole 32-byte slot: the record, then zero padding.
 __device__ __forceinline__ void st_rec(int4* p, int4 v) {
-  asm volatile("st.global.v4.s32 [%0], {%1,%2,%3,%4};"
-               :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+  asm volatile("st.global.v4.s32 [%0], {%1,%2,%3,%4};\n\t"
+               "st.global.v4.s32 [%0+16], {%5,%5,%5,%5};"
+               :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(0) : "memory");
 }
 __device__ __forceinline__ void st_rec_size(int4* p, int v) {
   asm volatile("st.global.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");

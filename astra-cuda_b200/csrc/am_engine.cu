@@ -143,6 +143,21 @@ int step_min_blocks() {
   return v;
 }
 
+// The step kernel for variant bits 1 = BBO outputs, 2 = int64 positions,
+// 4 = event counters.
+void launch_step(int variant, const am::StepArgs& a, dim3 grid, dim3 block, cudaStream_t s) {
+  switch (variant) {
+    case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
+    case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
+    case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
+    case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
+    case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
+    case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
+    case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
+    default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
+  }
+}
+
 int check_range(const am_dims& d, int32_t market0, int32_t count) {
   if (market0 < 0 || count < 0 || (int64_t)market0 + count > d.num_markets)
     return fail(AM_ERR_INVALID, "market range [%d, %d) outside [0, %d)", market0,
@@ -232,16 +247,7 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
     am::step_kernel<true, true, false, 4><<<grid, block, 0, s>>>(a);
     return launch_status("AddTwoSidedQuotes");
   }
-  switch (variant) {
-    case 0: am::step_kernel<false, false, false><<<grid, block, 0, s>>>(a); break;
-    case 1: am::step_kernel<true, false, false><<<grid, block, 0, s>>>(a); break;
-    case 2: am::step_kernel<false, true, false><<<grid, block, 0, s>>>(a); break;
-    case 3: am::step_kernel<true, true, false><<<grid, block, 0, s>>>(a); break;
-    case 4: am::step_kernel<false, false, true><<<grid, block, 0, s>>>(a); break;
-    case 5: am::step_kernel<true, false, true><<<grid, block, 0, s>>>(a); break;
-    case 6: am::step_kernel<false, true, true><<<grid, block, 0, s>>>(a); break;
-    default: am::step_kernel<true, true, true><<<grid, block, 0, s>>>(a); break;
-  }
+  launch_step(variant, a, grid, block, s);
   return launch_status("AddTwoSidedQuotes");
 }
 

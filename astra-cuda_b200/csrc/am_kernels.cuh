@@ -98,7 +98,7 @@ __device__ __forceinline__ int insert_order(const StepArgs& a, int4* rec, uint32
   const int slot = (int)((uint32_t)ns % (uint32_t)a.O);
   ns = wadd(ns, 1);
   v = make_int4(sz, cid, tid, make_meta(-1, px, side == 0 ? 1 : 0));
-  st_rec(rec + slot, v);
+  st_rec(rec_at(rec, slot), v);
   note_record(k, slot, v);
   linked = -1;
   const int old_tail = lv_tail(e);
@@ -110,7 +110,7 @@ __device__ __forceinline__ int insert_order(const StepArgs& a, int4* rec, uint32
     e = lv_make(lv_head(e), slot);
     became_head = false;
     if ((uint32_t)old_tail < (uint32_t)a.O) {
-      st_rec_next(rec + old_tail, slot);
+      st_rec_next(rec_at(rec, old_tail), slot);
       note_next(k, old_tail, slot);
       linked = old_tail;
     } else {
@@ -245,38 +245,38 @@ __device__ __forceinline__ void trading_epilogue(const StepArgs& a, int m, int b
   }
 }
 
-template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3, bool kTrading = false>
-__global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs a) {
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+// Event totals of the steps a thread ran (the event-counter variant).
+struct StepCounts {
+  int ins, fill, rm, empty, touch;
+};
+
+// One market's step, in the thread that owns it: AddTwoSidedQuotes +
+// MatchAllMarkets (market.cu:17-278), the optional fused GetBBOs, positions
+// and events, and the trading epilogue in the trading variant.
+template <bool kBBO, bool kPos, bool kEvents, bool kTrading>
+__device__ __forceinline__ void run_market(const StepArgs& a, const int m, StepCounts& ev) {
+  const size_t N = (size_t)a.N;
+  const int L = a.L, O = a.O, F = a.F;
   int e_ins = 0, e_fill = 0, e_rm = 0, e_empty = 0;
   unsigned long long touched = 0;
-  if (m < a.N) {
-    const size_t N = (size_t)a.N;
-    const int L = a.L, O = a.O, F = a.F;
-    // ---- first round trip: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
-    int bp, bs, ap, as, cid;
-    if constexpr (kTrading) {
-      // CopyCustomerPortfoliosTo(player_last_positions_), which the reference
-      // makes before its checks (high_low_trading.cc:257)
-      const TradingArgs& g = a.tr;
-      const int2* prow = reinterpret_cast<const int2*>(a.port) + (size_t)m * a.C;
-      int2* lrow = reinterpret_cast<int2*>(g.player_last_positions) + (size_t)m * a.C;
-      for (int p = 0; p < a.C; ++p) lrow[p] = prow[p];
-      if (g.checks && moves_fail(g.checks, g.V, g.T)) {  // the same answer in every thread
-        if (m == 0 && g.sticky && g.sticky[0] == 0) {
-          for (int k = 0; k < 8; ++k) g.sticky[1 + k] = (int)g.checks[k];
-          g.sticky[0] = 1;
-        }
-        return;
-      }
-      const int4 mv = ld_stream_v4(g.moves + m);  // {bid_px, ask_px, bid_sz, ask_sz}
-      bp = mv.x; ap = mv.y; bs = mv.z; as = mv.w;
-      cid = g.player;
-    } else {
-      bp = ld_stream(a.bid_px + m); bs = ld_stream(a.bid_sz + m);
-      ap = ld_stream(a.ask_px + m); as = ld_stream(a.ask_sz + m);
-      cid = ld_stream(a.cids + m);
-    }
+  // ---- first round trip: quotes, slot counter, occupancy, BBO cache (all coalesced) ----
+  int bp, bs, ap, as, cid;
+  if constexpr (kTrading) {
+    // CopyCustomerPortfoliosTo(player_last_positions_), which the reference
+    // makes before its checks (high_low_trading.cc:257)
+    const TradingArgs& g = a.tr;
+    const int2* prow = reinterpret_cast<const int2*>(a.port) + (size_t)m * a.C;
+    int2* lrow = reinterpret_cast<int2*>(g.player_last_positions) + (size_t)m * a.C;
+    for (int p = 0; p < a.C; ++p) lrow[p] = prow[p];
+    const int4 mv = ld_stream_v4(g.moves + m);  // {bid_px, ask_px, bid_sz, ask_sz}
+    bp = mv.x; ap = mv.y; bs = mv.z; as = mv.w;
+    cid = g.player;
+  } else {
+    bp = ld_stream(a.bid_px + m); bs = ld_stream(a.bid_sz + m);
+    ap = ld_stream(a.ask_px + m); as = ld_stream(a.ask_sz + m);
+    cid = ld_stream(a.cids + m);
+  }
+  {
     int ns = a.bk.slots[m];
     Mask128 bm{a.bk.mask[m], a.bk.mask[N + m]};
     Mask128 am_{a.bk.mask[2 * N + m], a.bk.mask[3 * N + m]};
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     k.cah = a.bk.bbo[2 * N + m];
     k.cas = a.bk.bbo[3 * N + m];
     uint32_t* lv = a.bk.levels + (size_t)m * (size_t)L * 2;
-    int4* rec = a.bk.orders + (size_t)m * (size_t)O;
+    int4* rec = a.bk.orders + (size_t)m * (size_t)O * kRecInt4;
 
     // market.cu:44 / :73 -- a negative price is undefined there; not added here
     const bool add_b = bs > 0 && bp < L && bp >= 0;
@@ -306,11 +306,11 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
     int4 PB = make_int4(0, 0, 0, 0), PA = PB;  // speculative head records ...
     int pb = -1, pa = -1;                      // ... of these slots (-1: none)
     if (add_a && ob >= 0 && ap <= ob && (uint32_t)k.cbh < (uint32_t)O) {
-      PB = ld_rec(rec + k.cbh);
+      PB = ld_rec(rec_at(rec, k.cbh));
       pb = k.cbh;
     }
     if (add_b && oa < L && bp >= oa && (uint32_t)k.cah < (uint32_t)O) {
-      PA = ld_rec(rec + k.cah);
+      PA = ld_rec(rec_at(rec, k.cah));
       pa = k.cah;
     }
 
@@ -374,14 +374,14 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
         if (k.ac == bslot) k.B = k.A;
         else if (pb == bslot) k.B = PB;
         else if (pa == bslot) k.B = PA;
-        else k.B = ld_rec(rec + bslot);
+        else k.B = ld_rec(rec_at(rec, bslot));
         k.bc = bslot;
       }
       if (k.ac != aslot) {
         if (k.bc == aslot) k.A = k.B;
         else if (pa == aslot) k.A = PA;
         else if (pb == aslot) k.A = PB;
-        else k.A = ld_rec(rec + aslot);
+        else k.A = ld_rec(rec_at(rec, aslot));
         k.ac = aslot;
       }
       pb = -1;  // prefetches serve the first iteration only
@@ -441,13 +441,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       int nb, na;
       if (bslot == aslot) {
         nb = na = wsub(wsub(B.x, q), q);
-        st_rec_size(rec + bslot, nb);
+        st_rec_size(rec_at(rec, bslot), nb);
         note_size(k, bslot, nb);
       } else {
         nb = wsub(B.x, q);
         na = wsub(A.x, q);
-        st_rec_size(rec + bslot, nb);
-        st_rec_size(rec + aslot, na);
+        st_rec_size(rec_at(rec, bslot), nb);
+        st_rec_size(rec_at(rec, aslot), na);
         note_size(k, bslot, nb);
         note_size(k, aslot, na);
       }
@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       const int h = lv_head(eb);
       if ((uint32_t)h < (uint32_t)O) {
         if (known_size(k, h, b_sz)) b_slot = h;
-        else if (kBBO) { b_sz = ld_rec_size(rec + h); b_slot = h; }
+        else if (kBBO) { b_sz = ld_rec_size(rec_at(rec, h)); b_slot = h; }
       } else {
         flag_state(a.bk.flag, kBadLevel);
       }
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
       const int h = lv_head(ea);
       if ((uint32_t)h < (uint32_t)O) {
         if (known_size(k, h, a_sz)) a_slot = h;
-        else if (kBBO) { a_sz = ld_rec_size(rec + h); a_slot = h; }
+        else if (kBBO) { a_sz = ld_rec_size(rec_at(rec, h)); a_slot = h; }
       } else {
         flag_state(a.bk.flag, kBadLevel);
       }
@@ -532,7 +532,40 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
                                              (ba < L && a_slot >= 0) ? ba : -1);
   }
   if (kEvents) {
-    int e_touch = __popcll(touched);
+    ev.ins += e_ins;
+    ev.fill += e_fill;
+    ev.rm += e_rm;
+    ev.empty += e_empty;
+    ev.touch += __popcll(touched);
+  }
+}
+
+// The lock-step step over all markets, one thread per market.
+template <bool kBBO, bool kPos, bool kEvents, int kMinBlocks = 3, bool kTrading = false>
+__global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs a) {
+  StepCounts ev{0, 0, 0, 0, 0};
+  if constexpr (kTrading) {
+    const TradingArgs& g = a.tr;
+    if (g.checks && moves_fail(g.checks, g.V, g.T)) {  // the same answer in every thread
+      // only CopyCustomerPortfoliosTo, which the reference makes before its
+      // checks (high_low_trading.cc:257)
+      const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+      for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < a.N; m += stride) {
+        const int2* prow = reinterpret_cast<const int2*>(a.port) + (size_t)m * a.C;
+        int2* lrow = reinterpret_cast<int2*>(g.player_last_positions) + (size_t)m * a.C;
+        for (int p = 0; p < a.C; ++p) lrow[p] = prow[p];
+      }
+      if (blockIdx.x == 0 && threadIdx.x == 0 && g.sticky && g.sticky[0] == 0) {
+        for (int k = 0; k < 8; ++k) g.sticky[1 + k] = (int)g.checks[k];
+        g.sticky[0] = 1;
+      }
+      return;
+    }
+  }
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m < a.N) run_market<kBBO, kPos, kEvents, kTrading>(a, m, ev);
+  if (kEvents) {
+    int e_ins = ev.ins, e_fill = ev.fill, e_rm = ev.rm, e_empty = ev.empty, e_touch = ev.touch;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       e_ins += __shfl_xor_sync(0xFFFFFFFFu, e_ins, o);
@@ -564,13 +597,13 @@ __global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, 
   const int bb = mhigh(bm), ba = mlow(am_, L);
   const int cb = bk.bbo[m], cbs = bk.bbo[n + m], ca = bk.bbo[2 * n + m], cas = bk.bbo[3 * n + m];
   const uint32_t* lv = bk.levels + (size_t)m * (size_t)L * 2;
-  const int4* rec = bk.orders + (size_t)m * (size_t)O;
+  const int4* rec = bk.orders + (size_t)m * (size_t)O * kRecInt4;
   int obp = -1, obs = 0, oap = -1, oas = 0;
   if (bb >= 0) {
     if (cb >= 0) { obp = bb; obs = cbs; }
     else {
       const int h = lv_head(lv[2 * bb]);
-      if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec + h); }
+      if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec_at(rec, h)); }
       else flag_state(bk.flag, kBadLevel);
     }
   }
@@ -578,7 +611,7 @@ __global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, 
     if (ca >= 0) { oap = ba; oas = cas; }
     else {
       const int h = lv_head(lv[2 * ba + 1]);
-      if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec + h); }
+      if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec_at(rec, h)); }
       else flag_state(bk.flag, kBadLevel);
     }
   }
@@ -795,7 +828,7 @@ __global__ void __launch_bounds__(kBlock) observation_kernel(const ObsArgs o) {
 __global__ void records_kernel(BookView bk, int64_t total) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x)
-    st_rec(bk.orders + i, make_int4(0, 0, 0, make_meta(-1, 0, 0)));
+    st_rec(bk.orders + kRecInt4 * i, make_int4(0, 0, 0, make_meta(-1, 0, 0)));
 }
 
 // ClearQuotes (market.cu:718-756) for the masked markets: slot counter 0,
@@ -827,10 +860,10 @@ __global__ void export_kernel(BookView bk, int N, int m0, int count, int L, int 
   const int64_t n_rec = (int64_t)count * O, n_lv = (int64_t)count * L;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int4* orders = bk.orders + (size_t)m0 * O;
+  const int4* orders = bk.orders + (size_t)m0 * O * kRecInt4;
   const uint32_t* levels = bk.levels + (size_t)m0 * L * 2;
   for (int64_t i = t0; i < n_rec; i += stride) {
-    const int4 v = orders[i];
+    const int4 v = orders[kRecInt4 * i];
     const uint32_t written = (uint32_t)bk.slots[m0 + i / O];  // slots used since the clear
     const bool fresh = written < (uint32_t)O && (uint32_t)(i % O) >= written;
     r.sizes[i] = v.x; r.cids[i] = v.y; r.tids[i] = v.z;
@@ -858,12 +891,12 @@ __global__ void import_kernel(BookView bk, int N, int m0, int count, int L, int 
   const int64_t n_rec = (int64_t)count * O, n_lv = (int64_t)count * L;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  int4* orders = bk.orders + (size_t)m0 * O;
+  int4* orders = bk.orders + (size_t)m0 * O * kRecInt4;
   uint32_t* levels = bk.levels + (size_t)m0 * L * 2;
   for (int64_t i = t0; i < n_rec; i += stride) {
     const int nx = r.next[i], px = r.prices[i], ib = r.is_bid[i] ? 1 : 0;
     if (!slot_ok(nx, O) || px < 0 || px > 255) flag_state(bk.flag, kBadImport);
-    orders[i] = make_int4(r.sizes[i], r.cids[i], r.tids[i],
+    orders[kRecInt4 * i] = make_int4(r.sizes[i], r.cids[i], r.tids[i],
                           make_meta(slot_ok(nx, O) ? nx : -1, px & 0xFF, ib));
   }
   for (int64_t i = t0; i < n_lv; i += stride) {

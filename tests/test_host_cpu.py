@@ -30,9 +30,9 @@ def test_native_dims_validation_without_gpu():
         assert _native.last_error()
     nbytes = ctypes.c_uint64(0)
     assert lib.am_book_bytes(ctypes.byref(D(1000, 128, 512, 512, 5)), ctypes.byref(nbytes)) == 0
-    # 16 B per order slot, 8 B per level, 52 B per market (slot counter, masks,
+    # 32 B per order slot, 8 B per level, 52 B per market (slot counter, masks,
     # BBO cache), 256-byte aligned blocks
-    per = 16 * 512 + 8 * 128 + 52
+    per = 32 * 512 + 8 * 128 + 52
     assert 1000 * per <= nbytes.value <= 1000 * per + 1536
 
 

@@ -166,10 +166,10 @@ __device__ __forceinline__ int4* rec_at(int4* rec, int slot) { return rec + kRec
 __device__ __forceinline__ const int4* rec_at(const int4* rec, int slot) {
   return rec + kRecInt4 * slot;
 }
-// A whole 32-byte slot: the record, then zero padding.
+// A whole 32-byte slot, the record then zero padding, in one 256-bit store
+// (one L2 request for the sector).
 __device__ __forceinline__ void st_rec(int4* p, int4 v) {
-  asm volatile("st.global.v4.s32 [%0], {%1,%2,%3,%4};\n\t"
-               "st.global.v4.s32 [%0+16], {%5,%5,%5,%5};"
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%5,%5,%5};"
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(0) : "memory");
 }
 __device__ __forceinline__ void st_rec_size(int4* p, int v) {
@@ -202,6 +202,12 @@ __device__ __forceinline__ int ld_after_red(const int* p) {
 // write-once outputs (fills, BBO): evict-first
 __device__ __forceinline__ void st_stream(int32_t* p, int v) {
   asm volatile("st.global.cs.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+// A 32-byte fill record in one 256-bit store (p 32-byte aligned).
+__device__ __forceinline__ void st_stream_v8(int4* p, int4 a, int4 b) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :: "l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z),
+                  "r"(b.w) : "memory");
 }
 __device__ __forceinline__ void st_stream_v4(int4* p, int4 v) {
   asm volatile("st.global.cs.v4.s32 [%0], {%1,%2,%3,%4};"

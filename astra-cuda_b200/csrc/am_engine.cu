@@ -220,6 +220,8 @@ int am_add_two_sided_quotes(const am_market* mk, const int32_t* bid_px, const in
     return fail(AM_ERR_INVALID, "quote pointers must not be NULL");
   if (d.num_markets > 0 && (!fill_counts || (!fills && d.max_active_fills_per_market > 0)))
     return fail(AM_ERR_INVALID, "fill buffers must not be NULL");
+  if (reinterpret_cast<uintptr_t>(fills) & 31)  // each record is one 256-bit store
+    return fail(AM_ERR_INVALID, "fills must be 32-byte aligned");
   const int n_bbo = (bbo_bid_px != nullptr) + (bbo_bid_sz != nullptr) + (bbo_ask_px != nullptr) +
                     (bbo_ask_sz != nullptr);
   if (n_bbo != 0 && n_bbo != 4)
@@ -486,6 +488,8 @@ int am_apply_player_trading(const am_market* mk, const am_trading_dims* td,
   if (!moves || !fill_counts || !bbos || (!fills && d.max_active_fills_per_market > 0))
     return fail(AM_ERR_INVALID, "moves, fills and bbos must not be NULL");
   if (!aligned16(moves)) return fail(AM_ERR_INVALID, "moves must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(fills) & 31)  // each record is one 256-bit store
+    return fail(AM_ERR_INVALID, "fills must be 32-byte aligned");
   if (((reinterpret_cast<uintptr_t>(st->player_last_positions) |
         reinterpret_cast<uintptr_t>(mk->portfolios)) & 7) != 0)
     return fail(AM_ERR_INVALID, "portfolio tensors must be 8-byte aligned");

@@ -405,10 +405,8 @@ __device__ __forceinline__ void run_market(const StepArgs& a, const int m, StepC
         const int4 f0a = ld_rec(base + 2 * (fc - 2)), f0b = ld_rec(base + 2 * (fc - 2) + 1);
         const int4 f1a = ld_rec(base + 2 * (fc - 1)), f1b = ld_rec(base + 2 * (fc - 1) + 1);
         for (int j = 0; j < R; j += 2) {
-          st_stream_v4(base + 2 * (fc + j), f0a);
-          st_stream_v4(base + 2 * (fc + j) + 1, f0b);
-          st_stream_v4(base + 2 * (fc + j + 1), f1a);
-          st_stream_v4(base + 2 * (fc + j + 1) + 1, f1b);
+          st_stream_v8(base + 2 * (fc + j), f0a, f0b);
+          st_stream_v8(base + 2 * (fc + j + 1), f1a, f1b);
         }
         // fill record: {price, size, taker, quoter} {quote size, taker tid, quote tid, is_sell}
         book_trade<kPos>(a, m, f0b.w ? f0a.z : f0a.w, f0b.w ? f0a.w : f0a.z, f0a.x, f0a.y, R / 2);
@@ -427,9 +425,9 @@ __device__ __forceinline__ void run_market(const StepArgs& a, const int m, StepC
       if constexpr (kTrading) last_px = price;
       int4* fr = reinterpret_cast<int4*>(a.fills + ((size_t)m * (size_t)F + (size_t)fc) * 8);
       // {price, size, taker cid, quoter cid} {quote size, taker tid, quote tid, is_sell_quote}
-      st_stream_v4(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y));
-      st_stream_v4(fr + 1, make_int4(bid_is_quote ? B.x : A.x, bid_is_quote ? A.z : B.z,
-                                     bid_is_quote ? B.z : A.z, bid_is_quote ? 0 : 1));
+      st_stream_v8(fr, make_int4(price, q, bid_is_quote ? A.y : B.y, bid_is_quote ? B.y : A.y),
+                   make_int4(bid_is_quote ? B.x : A.x, bid_is_quote ? A.z : B.z,
+                             bid_is_quote ? B.z : A.z, bid_is_quote ? 0 : 1));
       book_trade<kPos>(a, m, B.y, A.y, price, q, 1);  // buyer = bid's customer
       if (kEvents) {
         ++e_fill;

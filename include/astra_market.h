@@ -29,7 +29,8 @@
  *                 per-side level-occupancy masks.
  *  - portfolios:  int32 [N][C][2] (contracts, cash) -- the reference's
  *                 customer_portfolios_ layout (market.h:336-337).
- *  - fills:       int32 [N][F][8], one 32-byte record per fill: price, size,
+ *  - fills:       int32 [N][F][8], 32-byte aligned, one 32-byte record per
+ *                 fill (written as one 256-bit store): price, size,
  *                 taker customer id, quoter customer id, quote size, taker
  *                 tid, quote tid, is_sell_quote (0/1).  FillBatch's eight
  *                 [N][F] tensors (market.h:66-73) are strided views of it.

@@ -46,6 +46,12 @@ def test_null_and_range_errors_without_gpu():
     mk.book = 100  # misaligned
     assert lib.am_reset(ctypes.byref(mk), None) == _native.AM_ERR_INVALID
     assert "aligned" in _native.last_error()
+    # fill records are written as 256-bit stores: the buffer must be 32-byte aligned
+    mk.book = 256
+    q = 4096
+    assert lib.am_add_two_sided_quotes(ctypes.byref(mk), q, q, q, q, q, 0, q + 16, q, None, None,
+                                       None, None, None, None, None) == _native.AM_ERR_INVALID
+    assert "32-byte aligned" in _native.last_error()
 
 
 def test_vecmarket_constructor_checks_like_reference():

@@ -9,7 +9,9 @@
 //               (the match loop's pointer chase);
 //  * "store" -- independent stores to scattered sectors (fill and insert writes);
 //  * "rmw"   -- a load then a store of the same word (size updates);
-//  * "red"   -- fire-and-forget reductions (portfolio updates).
+//  * "red"   -- fire-and-forget reductions (portfolio updates);
+//  * "store32" -- independent 32-byte stores that cover a whole sector (fill
+//               records and 32-byte order slots): L2 needs nothing from DRAM.
 // All addresses are sector-aligned and uniformly spread; the result is
 // accesses per second for the whole grid, timed with CUDA events.
 #include <cuda_runtime.h>
@@ -44,8 +46,13 @@ __global__ void __launch_bounds__(256) probe_kernel(uint32_t* buf, uint64_t sect
       const uint32_t v = __ldcg(buf + i);
       __stcg(buf + i, v + 1);
       x += v + 1;
-    } else {  // reduction, no return value
+    } else if (kMode == 3) {  // reduction, no return value
       atomicAdd(buf + i, 1u);
+      x += 1;
+    } else {  // a whole sector in one 256-bit store
+      const uint32_t v = (uint32_t)x;
+      asm volatile("st.global.cg.v8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "l"(buf + i), "r"(v)
+                   : "memory");
       x += 1;
     }
   }
@@ -56,7 +63,7 @@ __global__ void __launch_bounds__(256) probe_kernel(uint32_t* buf, uint64_t sect
 
 extern "C" {
 
-// Runs mode 0..3 (load, store, rmw, red) over `bytes` of device memory with
+// Runs mode 0..4 (load, store, rmw, red, store32) over `bytes` of device memory with
 // `blocks` x 256 threads and `steps` accesses per thread; returns the kernel's
 // time in milliseconds (median of `reps`), or a negative value on error.
 float probe_run(int mode, uint64_t bytes, int blocks, int steps, int reps) {
@@ -77,7 +84,8 @@ float probe_run(int mode, uint64_t bytes, int blocks, int steps, int reps) {
       case 0: probe_kernel<0><<<blocks, 256>>>(buf, sectors, steps, sink); break;
       case 1: probe_kernel<1><<<blocks, 256>>>(buf, sectors, steps, sink); break;
       case 2: probe_kernel<2><<<blocks, 256>>>(buf, sectors, steps, sink); break;
-      default: probe_kernel<3><<<blocks, 256>>>(buf, sectors, steps, sink); break;
+      case 3: probe_kernel<3><<<blocks, 256>>>(buf, sectors, steps, sink); break;
+      default: probe_kernel<4><<<blocks, 256>>>(buf, sectors, steps, sink); break;
     }
     cudaEventRecord(b);
     cudaEventSynchronize(b);

@@ -482,7 +482,8 @@ def config_dict(cfg, args, markets, world):
 def sector_probe():
     """--sector-probe: scattered 32-byte-sector access rates of this GPU
     (astra-cuda_b200/measure/random_sector_probe.cu): dependent loads,
-    independent stores, load+store pairs and reductions, each uniformly spread
+    independent 4-byte stores, load+store pairs, reductions and whole-sector
+    32-byte stores, each uniformly spread
     over 4 GB, at 4 and 8 resident 256-thread blocks per SM.  The step kernel
     is made of exactly these accesses; the rates bound what it can reach."""
     import torch
@@ -499,12 +500,14 @@ def sector_probe():
     lib.probe_run.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
                               ctypes.c_int]
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    res = {"what": "scattered 4-byte accesses, one per 32-byte sector, uniform over 4 GB "
-                   "(far above L2), per-thread chains; accesses/s of the whole grid "
+    res = {"what": "scattered accesses (4 bytes; 32 for store_32B_sector), one per 32-byte "
+                   "sector, uniform over 4 GB (far above L2), per-thread chains; accesses/s "
+                   "of the whole grid "
                    "(median of 5 launches, CUDA events); sector_GB_s = accesses/s x 32 B",
            "sms": sms, "rates": []}
     steps = 64
-    for mode, name in enumerate(("dependent_load", "store", "load_then_store", "reduction")):
+    for mode, name in enumerate(("dependent_load", "store", "load_then_store", "reduction",
+                                 "store_32B_sector")):
         for per_sm in (4, 8):
             blocks = sms * per_sm
             ms = lib.probe_run(mode, 4 << 30, blocks, steps, 5)

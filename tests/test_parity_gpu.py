@@ -91,14 +91,15 @@ def test_odd_sizes():
     run_differential(g, 64, 128, 32, 8, 0, 50)           # C = 0
 
 
-@pytest.mark.parametrize("ci,n_full,sample", [(2, 1_000_000, 384), (3, 100_000, 384),
-                                              (4, 1_000_000, 384)])
+@pytest.mark.parametrize("ci,n_full,sample", [(2, 300_000, 384), (2, 1_000_000, 384),
+                                              (3, 100_000, 384), (4, 1_000_000, 384)])
 def test_full_size_sampled(ci, n_full, sample):
-    """Full market count; three contiguous samples (start, middle, end)
-    re-run on the oracle by global id and compared every step."""
+    """Full market count and the configuration's full step count (500, 2000,
+    2000); three contiguous samples (start, middle, end) re-run on the oracle
+    by global id and compared every 50 steps and at the end."""
     from astra_cuda import order_matching as aom, workloads
     c = cfg(ci)
-    steps = {2: 500, 3: 700, 4: 700}[ci]
+    steps = c["steps"]
     dev = torch.device("cuda:0")
     mkt = aom.VecMarket(n_full, c["L"], c["O"], c["F"], c["C"])
     fills, bbos = mkt.new_fill_batch(), mkt.new_bbo_batch()

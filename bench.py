@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--config", type=int, default=4)
     ap.add_argument("--markets", type=int, default=0, help="markets per GPU (default: the config's largest)")
     ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--latency-steps", type=int, default=256,
+                    help="further steps timed one by one for p50/p99 (0: skip)")
     ap.add_argument("--cpu-sample", type=int, default=262144,
                     help="markets in the CPU baseline sample (about 10 s of host work at config 4)")
     ap.add_argument("--trading-envs", type=int, default=1_000_000,
@@ -656,6 +658,30 @@ def main():
                 rg["speedup"] = round(rg["ms_per_step"] / (total_ms / K), 2)
         except Exception as ex:  # reported, never fatal for the GPU number
             extras["reference_gpu"] = {"error": repr(ex)}
+
+    # latency: per-step CUDA events over further steps of the same stream, so
+    # that p50/p99 rest on enough steps whatever K is
+    if not args.no_extras and args.latency_steps > 0:
+        lat, done = [], 0
+        while done < args.latency_steps:
+            k = min(64, args.latency_steps - done)
+            q = stream.take(k)
+            lev = [torch.cuda.Event(enable_timing=True) for _ in range(k + 1)]
+            torch.cuda.synchronize()
+            lev[0].record(cur)
+            for i in range(k):
+                step(q[i])
+                lev[i + 1].record(cur)
+            torch.cuda.synchronize()
+            lat += [lev[i].elapsed_time(lev[i + 1]) for i in range(k)]
+            done += k
+        del q
+        ls = sorted(lat)
+        extras["latency"] = {
+            "steps": len(ls), "p50_step_ms": ls[len(ls) // 2],
+            "p99_step_ms": ls[min(len(ls) - 1, int(0.99 * len(ls)))], "max_step_ms": ls[-1],
+            "what": f"per-step CUDA events over the {len(ls)} steps after the timed window "
+                    "(same stream continued), one launch each"}
 
     # e2e: quotes from pinned host memory every step, fill counts back
     e2e = None

@@ -433,7 +433,7 @@ def reference_gpu_leg(cfg, N, pre, qs, W, K, dev, our_counts, our_bbos):
     stream = workloads.DeviceQuoteStream(cfg["gen"], 0, N, dev)
     cur = torch.cuda.current_stream(dev)
     with ref_gpu.quiet():
-        t = 0
+        t, q = 0, None
         while t < pre:
             k = min(64, pre - t)
             q = stream.take(k)

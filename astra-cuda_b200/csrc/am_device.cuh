@@ -121,33 +121,9 @@ __device__ __forceinline__ int mlow(const Mask128& m, int none) {
   return m.lo ? __ffsll((long long)m.lo) - 1 : (m.hi ? 63 + __ffsll((long long)m.hi) : none);
 }
 
-// highest occupied level strictly below p, -1 if none (p <= 127)
-__device__ __forceinline__ int mhigh_below(const Mask128& m, int p) {
-  if (p <= 0) return -1;
-  if (p <= 64) {
-    const unsigned long long lo = p == 64 ? m.lo : (m.lo & ((1ull << p) - 1));
-    return lo ? 63 - __clzll((long long)lo) : -1;
-  }
-  const unsigned long long hi = m.hi & ((1ull << (p - 64)) - 1);
-  if (hi) return 127 - __clzll((long long)hi);
-  return m.lo ? 63 - __clzll((long long)m.lo) : -1;
-}
-// lowest occupied level strictly above p, `none` if none (p >= 0)
-__device__ __forceinline__ int mlow_above(const Mask128& m, int p, int none) {
-  if (p < 63) {
-    const unsigned long long lo = m.lo & ~((2ull << p) - 1);
-    if (lo) return __ffsll((long long)lo) - 1;
-    return m.hi ? 63 + __ffsll((long long)m.hi) : none;
-  }
-  if (p == 63) return m.hi ? 63 + __ffsll((long long)m.hi) : none;
-  if (p >= 127) return none;
-  const unsigned long long hi = m.hi & ~((2ull << (p - 64)) - 1);
-  return hi ? 63 + __ffsll((long long)hi) : none;
-}
-
 // ---- memory access ----
-// Order records are read as 16 bytes and written as 16 (insert), 4 (size) or
-// 2 (link) bytes.  These go through volatile asm with a memory clobber so the
+// Order records are read as 16 bytes and written as a whole 32-byte slot
+// (insert), 4 (size) or 2 (link) bytes.  These go through volatile asm with a memory clobber so the
 // compiler keeps their program order (they alias through different widths);
 // same-thread ordering in hardware does the rest.
 __device__ __forceinline__ int4 ld_rec(const int4* p) {

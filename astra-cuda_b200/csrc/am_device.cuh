@@ -121,7 +121,17 @@ __device__ __forceinline__ int mlow(const Mask128& m, int none) {
   return m.lo ? __ffsll((long long)m.lo) - 1 : (m.hi ? 63 + __ffsll((long long)m.hi) : none);
 }
 
+// The record of `slot` in a market's order array.
+__device__ __forceinline__ int4* rec_at(int4* rec, int slot) { return rec + kRecInt4 * slot; }
+__device__ __forceinline__ const int4* rec_at(const int4* rec, int slot) {
+  return rec + kRecInt4 * slot;
+}
+
 // ---- memory access ----
+// Every load and store the step makes goes through the helpers below.  A host
+// build that defines AM_HOST_EMULATION leaves them out and supplies plain C++
+// versions of the same names (the CPU test of the per-market step body).
+#ifndef AM_HOST_EMULATION
 // Order records are read as 16 bytes and written as a whole 32-byte slot
 // (insert), 4 (size) or 2 (link) bytes.  These go through volatile asm with a memory clobber so the
 // compiler keeps their program order (they alias through different widths);
@@ -136,11 +146,6 @@ __device__ __forceinline__ int ld_rec_size(const int4* p) {
   int r;
   asm volatile("ld.global.s32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
   return r;
-}
-// The record of `slot` in a market's order array.
-__device__ __forceinline__ int4* rec_at(int4* rec, int slot) { return rec + kRecInt4 * slot; }
-__device__ __forceinline__ const int4* rec_at(const int4* rec, int slot) {
-  return rec + kRecInt4 * slot;
 }
 // A whole 32-byte slot, the record then zero padding, in one 256-bit store
 // (one L2 request for the sector).
@@ -199,6 +204,7 @@ __device__ __forceinline__ void red_add64(long long* p, long long v) {
 }
 
 __device__ __forceinline__ void flag_state(int32_t* flag, int code) { atomicOr(flag, code); }
+#endif  // AM_HOST_EMULATION
 
 // state-check codes (OR-ed into the flag word)
 constexpr int kBadSlot = 1;   // a level head/tail or link outside [-1, O)

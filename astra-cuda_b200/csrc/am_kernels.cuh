@@ -59,41 +59,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) step_kernel(const StepArgs
   }
 }
 
-// get_bbo_kernel (market.cu:280-320) from the occupancy masks and the BBO
-// cache the last step left; only a side whose cached head is unknown reads
-// its level entry and head record.
+// get_bbo_kernel (market.cu:280-320), one thread per market (bbo_market).
 __global__ void __launch_bounds__(kBlock) bbo_kernel(BookView bk, int N, int L, int O,
                                                      int32_t* bbp, int32_t* bbs, int32_t* bap,
                                                      int32_t* bas) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= N) return;
-  const size_t n = (size_t)N;
-  const Mask128 bm{bk.mask[m], bk.mask[n + m]}, am_{bk.mask[2 * n + m], bk.mask[3 * n + m]};
-  const int bb = mhigh(bm), ba = mlow(am_, L);
-  const int cb = bk.bbo[m], cbs = bk.bbo[n + m], ca = bk.bbo[2 * n + m], cas = bk.bbo[3 * n + m];
-  const uint32_t* lv = bk.levels + (size_t)m * (size_t)L * 2;
-  const int4* rec = bk.orders + (size_t)m * (size_t)O * kRecInt4;
-  int obp = -1, obs = 0, oap = -1, oas = 0;
-  if (bb >= 0) {
-    if (cb >= 0) { obp = bb; obs = cbs; }
-    else {
-      const int h = lv_head(lv[2 * bb]);
-      if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec_at(rec, h)); }
-      else flag_state(bk.flag, kBadLevel);
-    }
-  }
-  if (ba < L) {
-    if (ca >= 0) { oap = ba; oas = cas; }
-    else {
-      const int h = lv_head(lv[2 * ba + 1]);
-      if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec_at(rec, h)); }
-      else flag_state(bk.flag, kBadLevel);
-    }
-  }
-  st_stream(bbp + m, obp);
-  st_stream(bbs + m, obs);
-  st_stream(bap + m, oap);
-  st_stream(bas + m, oas);
+  bbo_market(bk, N, L, O, m, bbp, bbs, bap, bas);
 }
 
 // update_last_prices_kernel (market.cu:767-786) on the packed fill records.

@@ -1,7 +1,8 @@
-// The per-market body of the matching step: one thread's work on one market
-// (AddTwoSidedQuotes + MatchAllMarkets, market.cu:17-278, with the fused
-// GetBBOs, int64 positions, event counts and the player-trading epilogue).
-// The launch around it is step_kernel in am_kernels.cuh.
+// The per-market bodies of the matching step and of GetBBOs: one thread's
+// work on one market (AddTwoSidedQuotes + MatchAllMarkets, market.cu:17-278,
+// with the fused GetBBOs, int64 positions, event counts and the
+// player-trading epilogue; and the standalone GetBBOs, market.cu:280-320).
+// The launches around them are step_kernel and bbo_kernel in am_kernels.cuh.
 //
 // Everything here reaches memory only through the access helpers of
 // am_device.cuh, so the same source also compiles with a host C++ compiler
@@ -524,6 +525,41 @@ __device__ __forceinline__ void run_market(const StepArgs& a, const int m, StepC
     ev.empty += e_empty;
     ev.touch += __popcll(touched);
   }
+}
+
+// get_bbo_kernel (market.cu:280-320) for market m, from the occupancy masks
+// and the BBO cache the last step left; only a side whose cached head is
+// unknown reads its level entry and head record.
+__device__ __forceinline__ void bbo_market(const BookView& bk, int N, int L, int O, int m,
+                                           int32_t* bbp, int32_t* bbs, int32_t* bap,
+                                           int32_t* bas) {
+  const size_t n = (size_t)N;
+  const Mask128 bm{bk.mask[m], bk.mask[n + m]}, am_{bk.mask[2 * n + m], bk.mask[3 * n + m]};
+  const int bb = mhigh(bm), ba = mlow(am_, L);
+  const int cb = bk.bbo[m], cbs = bk.bbo[n + m], ca = bk.bbo[2 * n + m], cas = bk.bbo[3 * n + m];
+  const uint32_t* lv = bk.levels + (size_t)m * (size_t)L * 2;
+  const int4* rec = bk.orders + (size_t)m * (size_t)O * kRecInt4;
+  int obp = -1, obs = 0, oap = -1, oas = 0;
+  if (bb >= 0) {
+    if (cb >= 0) { obp = bb; obs = cbs; }
+    else {
+      const int h = lv_head(lv[2 * bb]);
+      if ((uint32_t)h < (uint32_t)O) { obp = bb; obs = ld_rec_size(rec_at(rec, h)); }
+      else flag_state(bk.flag, kBadLevel);
+    }
+  }
+  if (ba < L) {
+    if (ca >= 0) { oap = ba; oas = cas; }
+    else {
+      const int h = lv_head(lv[2 * ba + 1]);
+      if ((uint32_t)h < (uint32_t)O) { oap = ba; oas = ld_rec_size(rec_at(rec, h)); }
+      else flag_state(bk.flag, kBadLevel);
+    }
+  }
+  st_stream(bbp + m, obp);
+  st_stream(bbs + m, obs);
+  st_stream(bap + m, oap);
+  st_stream(bas + m, oas);
 }
 
 }  // namespace am

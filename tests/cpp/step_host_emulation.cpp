@@ -1,12 +1,12 @@
-// Host build of the matching step's per-market body -- TEST INFRASTRUCTURE
-// ONLY.  It compiles astra-cuda_b200/csrc/am_step.cuh, the exact source the
-// CUDA library's step_kernel runs in each thread, with a host C++ compiler:
-// AM_HOST_EMULATION replaces the device access helpers of am_device.cuh
-// (inline-PTX loads, 256-bit stores, RED adds) with plain C++ ones of the same
-// meaning, and the markets run one after another instead of one per thread.
-// tests/test_step_host_cpu.py drives it through the C functions below and
-// compares every output with the CPU oracle.  Nothing in the product loads
-// this file or what it builds.
+// Host build of the matching engine's per-market bodies -- TEST
+// INFRASTRUCTURE ONLY.  It compiles astra-cuda_b200/csrc/am_step.cuh, the
+// exact source the CUDA library's step_kernel and bbo_kernel run in each
+// thread, with a host C++ compiler: AM_HOST_EMULATION replaces the device
+// access helpers of am_device.cuh (inline-PTX loads, 256-bit stores, RED adds)
+// with plain C++ ones of the same meaning, and the markets run one after
+// another instead of one per thread.  tests/test_step_host_cpu.py drives it
+// through the C functions below and compares every output with the CPU
+// oracle.  Nothing in the product loads this file or what it builds.
 #include <algorithm>
 #include <cstddef>
 #include <cstdint>
@@ -140,6 +140,15 @@ int hs_step(void* book, int N, int L, int O, int F, int C, int32_t* port, const 
     default: run_all<true, true, true, false>(a, events); break;
   }
   return *a.bk.flag;
+}
+
+// GetBBOs over all markets (what am_get_bbos launches): bbo int32 [4][N].
+// Returns the book's state-check flag.
+int hs_get_bbos(void* book, int N, int L, int O, int32_t* bbo) {
+  const am::BookView v = am::view_of(book, N, L, O);
+  const size_t n = (size_t)N;
+  for (int m = 0; m < N; ++m) am::bbo_market(v, N, L, O, m, bbo, bbo + n, bbo + 2 * n, bbo + 3 * n);
+  return *v.flag;
 }
 
 // One player-trading move with passing checks (what am_apply_player_trading

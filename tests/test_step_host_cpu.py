@@ -67,6 +67,8 @@ def lib(tmp_path_factory):
     h.hs_step.restype = ctypes.c_int
     h.hs_step.argtypes = ([ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p] * 6 +
                           [ctypes.c_int32] + [ctypes.c_void_p] * 5)
+    h.hs_get_bbos.restype = ctypes.c_int
+    h.hs_get_bbos.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 3 + [ctypes.c_void_p]
     h.hs_trading_step.restype = ctypes.c_int
     h.hs_trading_step.argtypes = ([ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p] * 2 +
                                   [ctypes.c_int32] * 5 + [ctypes.c_void_p] * 12)
@@ -111,6 +113,10 @@ class HostMarket:
                               ptr(self.port), *[ptr(x) for x in q], base_tid, ptr(self.fills),
                               ptr(self.counts), ptr(self.bbo) if bbo else None, ptr(positions),
                               ptr(events))
+        assert rc == 0, f"state-check flag {rc}"
+
+    def get_bbos(self):
+        rc = self.lib.hs_get_bbos(self.blob.ctypes.data, self.N, self.L, self.O, ptr(self.bbo))
         assert rc == 0, f"state-check flag {rc}"
 
     def state(self):
@@ -190,10 +196,12 @@ def compare_state(hm, orc, where):
                                  f"oracle {o[idx]}")
 
 
-def run_pair(lib, N, L, O, F, C, steps, quotes, bbo=True, positions=False, events=True,
+def run_pair(lib, N, L, O, F, C, steps, quotes, bbo="fused", positions=False, events=True,
              state_every=0):
     """Step the host body and the oracle on the same quotes; compare after
-    every step.  `quotes(t)` returns the five int32 [N] arrays of step t."""
+    every step.  `quotes(t)` returns the five int32 [N] arrays of step t;
+    bbo: "fused" (from the step), "separate" (GetBBOs after a step that
+    writes none) or "none"."""
     hm = HostMarket(lib, N, L, O, F, C)
     orc = oracle.OracleMarket(N, L, O, F, C)
     ofills, obbos = orc.new_fill_batch(), orc.new_bbo_batch()
@@ -203,11 +211,13 @@ def run_pair(lib, N, L, O, F, C, steps, quotes, bbo=True, positions=False, event
     oev = np.zeros(5, np.int64)
     for t in range(steps):
         q = quotes(t)
-        hm.step(q, orc.global_tid_counter, bbo=bbo, positions=pos, events=ev)
+        hm.step(q, orc.global_tid_counter, bbo=bbo == "fused", positions=pos, events=ev)
+        if bbo == "separate":
+            hm.get_bbos()
         e = orc.add_two_sided_quotes(*q, ofills, pos64=opos)
         oev += [e["n_ins"], e["n_fill"], e["n_rm"], e["n_empty"], e["n_touch"]]
         compare_fills(hm, ofills, f"step {t}")
-        if bbo:
+        if bbo != "none":
             orc.get_bbos(obbos)
             compare_bbo(hm, obbos, f"step {t}")
         if state_every and (t + 1) % state_every == 0:
@@ -229,12 +239,15 @@ def generated(gen, N):
 
 # (config, markets, bbo, positions): every configuration through its full step count
 CONFIG_CASES = [
-    (0, 64, True, False),
-    (0, 64, False, False),   # no BBO output: the cache keeps unknown sizes unknown
-    (1, 256, True, False),   # the 1024-slot ring wraps
-    (2, 256, True, False),
-    (3, 256, True, False),   # contention: deep FIFOs, partial fills, ring wrap
-    (4, 512, True, True),    # rollout shape with int64 positions; 512-slot ring and budget
+    (0, 64, "fused", False),
+    (0, 64, "separate", False),  # the step leaves sizes it did not load unknown in the cache
+    (0, 64, "none", False),
+    (1, 256, "fused", False),    # the 1024-slot ring wraps
+    (1, 256, "separate", False),
+    (2, 256, "fused", False),
+    (3, 256, "fused", False),    # contention: deep FIFOs, partial fills, ring wrap
+    (3, 256, "separate", False),
+    (4, 512, "fused", True),     # rollout shape with int64 positions; 512-slot ring and budget
 ]
 
 
@@ -254,7 +267,8 @@ def test_tight_rings_and_budgets(lib, O, F):
     gen = dict(seed=O * 100 + F, kind=1, walk=0, mid_lo=64, mid_hi=64, cid_cycle=3)
     run_pair(lib, 48, 128, O, F, 3, 160, generated(gen, 48), positions=True, state_every=40)
     gen = dict(seed=O * 100 + F + 7, kind=0, walk=2, mid_lo=16, mid_hi=112, cid_cycle=5)
-    run_pair(lib, 48, 128, O, F, 5, 120, generated(gen, 48), bbo=(F % 2 == 0), positions=True)
+    run_pair(lib, 48, 128, O, F, 5, 120, generated(gen, 48),
+             bbo="fused" if F % 2 == 0 else "separate", positions=True)
 
 
 def wild_quotes(rng, N, L, C, crossing):
@@ -290,8 +304,8 @@ def test_random_shapes_and_wild_inputs(lib, seed):
     steps = int(rng.integers(20, 120))
     crossing = bool(rng.random() < 0.7)
     qs = [wild_quotes(rng, N, L, C, crossing) for _ in range(steps)]
-    run_pair(lib, N, L, O, F, C, steps, lambda t: qs[t], bbo=bool(seed % 3), positions=bool(seed % 2),
-             state_every=10)
+    run_pair(lib, N, L, O, F, C, steps, lambda t: qs[t], bbo=("none", "fused", "separate")[seed % 3],
+             positions=bool(seed % 2), state_every=10)
 
 
 # ---- the player-trading variant ----

@@ -36,6 +36,7 @@ import math
 import torch
 
 from . import _native
+from ._trace import traced
 from .order_matching import VecMarket, _check_op, _fatal, _i32_wrap, _raw_stream
 
 _lib = _native.lib()
@@ -156,6 +157,7 @@ class HighLowTradingState:
                 _fatal(f"{name} must be an int32 tensor of shape {list(shape)} on device "
                        f"{self.device_id}" + ("" if name in strided else ", contiguous"))
 
+    @traced("ApplyPlayerTrading")
     def apply_player_trading(self, move: torch.Tensor, *, check: str = "sync") -> None:
         """ApplyPlayerTrading (high_low_trading.cc:247-329) for the current
         player: move int32 [N, 4] = (bid_px, ask_px, bid_sz, ask_sz).
@@ -245,6 +247,7 @@ class HighLowTradingState:
         """ObservationTensorShape (:506-508): [N, 6 + 1 + 6P + 5]."""
         return [self.num_envs, 6 + 1 + 6 * self.num_players + 5]
 
+    @traced("FillObservationTensor")
     def fill_observation_tensor(self, player: int, values: torch.Tensor) -> None:
         """FillObservationTensor (:510-601) for `player` into values, float32
         [N, 12 + 6P] (other float dtypes receive a copy), in one launch."""
@@ -304,6 +307,7 @@ class HighLowTradingState:
         _check_op(reward_buffer.size(0), "==", self.num_envs, "reward_buffer.size(0)", "num_envs_")
         reward_buffer.copy_(self.rewards_since_last_action[:, player_id])
 
+    @traced("FillReturns")
     def fill_returns(self, returns_buffer: torch.Tensor) -> None:
         """FillReturns (:345-371): cash + contracts * settlement value, minus
         max_contract_value per contract a customer misses its target by; one
@@ -327,6 +331,7 @@ class HighLowTradingState:
             returns_buffer.copy_(out)
 
     # --- DoReset (high_low_trading.cc:373-392), trading tensors ---
+    @traced("DoReset")
     def reset(self) -> None:
         for t in (self.contract_values, self.contract_high_settle, self.player_permutation,
                   self.target_positions, self.player_last_positions,

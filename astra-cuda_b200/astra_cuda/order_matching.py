@@ -36,6 +36,7 @@ import ctypes
 import torch
 
 from . import _native
+from ._trace import traced
 
 # market.h:56-61, exposed at market_bindings.cc:67-72
 MAX_MARKETS = 2048 * 2048
@@ -164,6 +165,7 @@ class BBOBatch:
         """BBOBatch::Reset (market.cu:788-796): all five rows to 0."""
         self.storage.zero_()
 
+    @traced("UpdateLastPrices")
     def update_last_prices(self, fills: FillBatch) -> None:
         """BBOBatch::UpdateLastPrices (market.cu:798-825): where a market
         filled this step, last price = the price of its last fill."""
@@ -277,6 +279,7 @@ class VecMarket:
         return BBOBatch(self.num_markets, self.device)
 
     # --- the step ---
+    @traced("AddTwoSidedQuotes")
     def add_two_sided_quotes(self, bid_px, bid_sz, ask_px, ask_sz, customer_ids, fills, *,
                              bbos=None, positions=None, events=None):
         """Add two-sided quotes (bid and ask) for all markets in parallel
@@ -334,6 +337,7 @@ class VecMarket:
         _check(rc, "AddTwoSidedQuotes")
         self._tid = _i32_wrap(self._tid + 2)            # market.cu:531
 
+    @traced("GetBBOs")
     def get_bbos(self, bbos: BBOBatch) -> None:
         """Populate the best bid and offer (BBO) for all markets"""
         if not isinstance(bbos, BBOBatch):
@@ -356,11 +360,13 @@ class VecMarket:
         _check_op(buffer.size(2), "==", 2, "buffer.size(2)", "2")
         buffer.copy_(self._portfolios, non_blocking=False)
 
+    @traced("Reset")
     def reset(self) -> None:
         """VecMarket::Reset (market.cu:693-716)."""
         _check(_lib.am_reset(self._mkref, self._stream()), "Reset")
         self._tid = 0
 
+    @traced("ClearQuotes")
     def clear_quotes(self, reset_indices: torch.Tensor) -> None:
         """VecMarket::ClearQuotes (market.cu:718-756)."""
         _check_op(reset_indices.dim(), "==", 1, "reset_indices.dim()", "1")

@@ -115,6 +115,17 @@ void hs_book_init(void* book, int64_t N, int64_t L, int64_t O) {
     am::st_rec(v.orders + am::kRecInt4 * i, make_int4(0, 0, 0, am::make_meta(-1, 0, 0)));
 }
 
+// What am_reset does (VecMarket::Reset, market.cu:693-716): slot counters and
+// masks 0, BBO cache unknown, portfolios 0; the flag, the level entries and the
+// records are kept.
+void hs_reset(void* book, int64_t N, int64_t L, int64_t O, int32_t* port, int64_t C) {
+  const am::Layout l = am::layout_of(N, L, O);
+  char* b = static_cast<char*>(book);
+  std::memset(b + l.off_slots, 0, l.off_levels - l.off_slots);
+  std::memset(b + l.off_bbo, 0xFF, l.off_orders - l.off_bbo);
+  if (N > 0 && C > 0) std::memset(port, 0, (size_t)N * (size_t)C * 8);
+}
+
 // One lock-step call over all markets (what am_add_two_sided_quotes launches).
 // bbo: int32 [4][N] or NULL; positions: int64 [N][C][2] or NULL; events:
 // int64 [5] totals to add to, or NULL.  Returns the book's state-check flag.

@@ -15,8 +15,11 @@ reference's layout (decoded here from the packed book independently of the
 library's export kernel).  They cover every benchmark configuration through
 its full step count, tight rings and fill budgets, and seeded random inputs
 outside the benchmarks' ranges (negative and out-of-range prices, sizes and
-customer ids, int32 extremes).  The GPU tests check the same properties on
-the device; these keep the kernel's logic checked on every CPU run.
+customer ids, int32 extremes).  The body also replays the outputs recorded
+from the reference's own engine and trading game
+(``tests/golden/ref_*_fixtures.npz``) with no oracle in between.  The GPU
+tests check the same properties on the device; these keep the kernel's logic
+checked on every CPU run.
 """
 import ctypes
 import importlib.util
@@ -67,6 +70,8 @@ def lib(tmp_path_factory):
     h.hs_step.restype = ctypes.c_int
     h.hs_step.argtypes = ([ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p] * 6 +
                           [ctypes.c_int32] + [ctypes.c_void_p] * 5)
+    h.hs_reset.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p,
+                                                                       ctypes.c_int64]
     h.hs_get_bbos.restype = ctypes.c_int
     h.hs_get_bbos.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 3 + [ctypes.c_void_p]
     h.hs_trading_step.restype = ctypes.c_int
@@ -114,6 +119,9 @@ class HostMarket:
                               ptr(self.counts), ptr(self.bbo) if bbo else None, ptr(positions),
                               ptr(events))
         assert rc == 0, f"state-check flag {rc}"
+
+    def reset(self):
+        self.lib.hs_reset(self.blob.ctypes.data, self.N, self.L, self.O, ptr(self.port), self.C)
 
     def get_bbos(self):
         rc = self.lib.hs_get_bbos(self.blob.ctypes.data, self.N, self.L, self.O, ptr(self.bbo))
@@ -369,3 +377,121 @@ def test_trading_moves_match_the_trading_oracle(lib, P, S, V, T, layout):
         np.testing.assert_array_equal(hm.port, orc.market.customer_portfolios,
                                       err_msg=f"portfolios {where}")
     compare_state(hm, orc.market, "end of episode")
+
+
+# ---- the reference's own recorded outputs ----
+
+GOLDEN = os.path.join(HERE, "golden")
+
+
+def _fixture(name):
+    path = os.path.join(GOLDEN, name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not recorded")
+    with np.load(path) as z:
+        return {k: z[k] for k in z.files}
+
+
+def _runs(z):
+    return sorted({k.split("/")[0] for k in z if k.endswith("/dims")})
+
+
+def _written(rec, counts, F):
+    """The fixture's fill slots (at most 32) with those a step did not write zeroed."""
+    k = min(F, 32)
+    rec = np.array(rec[:, :k], copy=True)
+    w = np.where(counts < 0, F, counts)
+    rec[np.arange(k)[None, :] >= w[:, None]] = 0
+    return rec
+
+
+def _same(name, got, want, where):
+    got, want = np.asarray(got), np.asarray(want)
+    if got.dtype == np.bool_:
+        got = got.astype(want.dtype)
+    assert got.shape == want.shape, (name, where, got.shape, want.shape)
+    if not np.array_equal(got, want):
+        idx = tuple(np.argwhere(got != want)[0])
+        raise AssertionError(f"{name} {where}: first diff at {idx}: host body {got[idx]}, "
+                             f"reference {want[idx]}")
+
+
+def _i32(v):
+    return int(np.int64(v).astype(np.int32))
+
+
+@pytest.mark.parametrize("bbo", ["fused", "separate"])
+def test_host_body_reproduces_reference_market_runs(lib, bbo):
+    """The reference's VecMarket, recorded on a B200 (config 0; a 16-slot ring
+    with 6 fill slots that reaches self-loops, negative sizes and the -1
+    sentinel), replayed through the kernel's body: every step's counts, fills
+    and BBOs, then the whole book, portfolios and tid counter."""
+    z = _fixture("ref_market_fixtures.npz")
+    for run in _runs(z):
+        N, L, O, F, C = (int(x) for x in z[f"{run}/dims"])
+        hm = HostMarket(lib, N, L, O, F, C)
+        tid = 0
+        for t, q in enumerate(z[f"{run}/quotes"]):
+            hm.step(list(q), tid, bbo=bbo == "fused")
+            if bbo == "separate":
+                hm.get_bbos()
+            tid = _i32(tid + 2)  # market.cu:531
+            where = f"{run} step {t} ({bbo})"
+            _same("fill_counts", hm.counts, z[f"{run}/fill_counts"][t], where)
+            _same("fills", _written(hm.fills, hm.counts, F), z[f"{run}/fills"][t], where)
+            _same("bbos", hm.bbo[:4], z[f"{run}/bbos"][t], where)
+        st = hm.state()
+        for k in STATE_KEYS[:-1]:
+            _same(k, st[k], z[f"{run}/book/{k}"], f"{run} end")
+        _same("portfolios", hm.port, z[f"{run}/portfolios"], f"{run} end")
+        assert tid == int(z[f"{run}/tid"])
+
+
+def test_host_trading_body_reproduces_reference_game(lib):
+    """The reference's high-low trading game, recorded on a B200 (three game
+    shapes, fill budget 2 so it overflows, two episodes each with Reset
+    between), replayed through the trading variant of the kernel's body:
+    every move's fills, BBOs and last prices, portfolios, the portfolio copy,
+    immediate rewards and rewards since the last action, then the history."""
+    z = _fixture("ref_trading_fixtures.npz")
+    for run in _runs(z):
+        if run == "reject":
+            continue
+        N, P, S, V, T, _ = (int(x) for x in z[f"{run}/dims"])
+        L, O, F = V + 1, P * S * 2, min(P * S * 2, T * 2)  # high_low_trading.cc:57-69
+        hm = HostMarket(lib, N, L, O, F, P)
+        for ep in (0, 1):
+            pre = f"{run}/ep{ep}"
+            if ep:
+                hm.reset()
+            hm.bbo[...] = 0
+            cv = aligned((N, 3), np.int32, z[f"{pre}/contract_values"])
+            tgt = aligned((N, P), np.int32, z[f"{pre}/target_positions"])
+            last_pos = aligned((N, P, 2), np.int32)
+            imm = aligned((N, P), np.int32)
+            rsla = aligned((N, P), np.int32)
+            pcot, ps = _env_minor((N, P, S, 6), (2, 3, 1, 0))
+            mcot, ms = _env_minor((N, P * S, 3), (1, 2, 0))
+            tid = 0
+            for t, mv in enumerate(z[f"{pre}/moves"]):
+                moves = aligned((N, 4), np.int32, mv)
+                rc = lib.hs_trading_step(hm.blob.ctypes.data, N, L, O, F, P, ptr(hm.port),
+                                         ptr(moves), t, S, V, T, tid, ptr(hm.fills),
+                                         ptr(hm.counts), ptr(hm.bbo), ptr(cv), ptr(tgt),
+                                         ptr(last_pos), pcot.ctypes.data, ps.ctypes.data,
+                                         mcot.ctypes.data, ms.ctypes.data, ptr(imm), ptr(rsla))
+                assert rc == 0
+                tid = _i32(tid + 2)
+                where = f"{pre} move {t}"
+                _same("fill_counts", hm.counts, z[f"{pre}/fill_counts"][t], where)
+                _same("fills", _written(hm.fills, hm.counts, F), z[f"{pre}/fills"][t], where)
+                _same("bbos", hm.bbo, z[f"{pre}/bbos"][t], where)
+                _same("portfolios", hm.port, z[f"{pre}/customer_portfolios"][t], where)
+                _same("player_last_positions", last_pos, z[f"{pre}/player_last_positions"][t], where)
+                _same("immediate_rewards", imm, z[f"{pre}/immediate_rewards"][t], where)
+                _same("rewards_since_last_action", rsla, z[f"{pre}/rewards_since_last_action"][t],
+                      where)
+            _same("player_contract_over_time", pcot, z[f"{pre}/player_contract_over_time"],
+                  f"{pre} end")
+            _same("market_contract_over_time", mcot, z[f"{pre}/market_contract_over_time"],
+                  f"{pre} end")

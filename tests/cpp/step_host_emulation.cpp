@@ -153,6 +153,13 @@ int hs_step(void* book, int N, int L, int O, int F, int C, int32_t* port, const 
   return *a.bk.flag;
 }
 
+// The trading step's verdict on the eight check words of move_check_kernel
+// (minima of bid_px, ask_px, bid_sz, ask_sz, then their maxima, each stored
+// as x ^ 0x80000000): 1 when a check of high_low_trading.cc:265-272 fails.
+int hs_moves_fail(const uint32_t* words, int32_t V, int32_t T) {
+  return am::moves_fail(words, V, T) ? 1 : 0;
+}
+
 // GetBBOs over all markets (what am_get_bbos launches): bbo int32 [4][N].
 // Returns the book's state-check flag.
 int hs_get_bbos(void* book, int N, int L, int O, int32_t* bbo) {

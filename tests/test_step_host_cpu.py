@@ -72,6 +72,8 @@ def lib(tmp_path_factory):
                           [ctypes.c_int32] + [ctypes.c_void_p] * 5)
     h.hs_reset.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p,
                                                                        ctypes.c_int64]
+    h.hs_moves_fail.restype = ctypes.c_int
+    h.hs_moves_fail.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32]
     h.hs_get_bbos.restype = ctypes.c_int
     h.hs_get_bbos.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 3 + [ctypes.c_void_p]
     h.hs_trading_step.restype = ctypes.c_int
@@ -377,6 +379,26 @@ def test_trading_moves_match_the_trading_oracle(lib, P, S, V, T, layout):
         np.testing.assert_array_equal(hm.port, orc.market.customer_portfolios,
                                       err_msg=f"portfolios {where}")
     compare_state(hm, orc.market, "end of episode")
+
+
+def test_move_checks_verdict(lib):
+    """The step's reading of the check words (moves_fail) against the eight
+    checks of ApplyPlayerTrading (high_low_trading.cc:265-272) on the column
+    minima and maxima: prices in [1, V], sizes in [0, T], boundaries and int32
+    extremes included."""
+    rng = np.random.default_rng(7)
+    edge = [-2**31, -1, 0, 1, 2, 4, 5, 6, 29, 30, 31, 2**31 - 1]
+    for case in range(4000):
+        V, T = int(rng.choice([1, 5, 30, 100])), int(rng.choice([0, 1, 5, 50]))
+        vals = [int(rng.choice(edge)) if rng.random() < 0.3 else int(rng.integers(-3, V + 4))
+                for _ in range(4)]
+        vals += [int(rng.choice(edge)) if rng.random() < 0.3 else int(rng.integers(-3, V + 4))
+                 for _ in range(4)]
+        mn, mx = vals[:4], vals[4:]  # bid_px, ask_px, bid_sz, ask_sz
+        ok = (mn[0] > 0 and mn[1] > 0 and mx[0] <= V and mx[1] <= V and mn[2] >= 0
+              and mn[3] >= 0 and mx[2] <= T and mx[3] <= T)
+        words = np.array([(v & 0xFFFFFFFF) ^ 0x80000000 for v in mn + mx], np.uint32)
+        assert lib.hs_moves_fail(words.ctypes.data, V, T) == (0 if ok else 1), (V, T, mn, mx)
 
 
 # ---- the reference's own recorded outputs ----

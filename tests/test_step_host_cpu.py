@@ -303,7 +303,7 @@ def wild_quotes(rng, N, L, C, crossing):
     return [bp, bs, ap, as_, cid]
 
 
-@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("seed", range(150))
 def test_random_shapes_and_wild_inputs(lib, seed):
     rng = np.random.default_rng(1000 + seed)
     L = int(rng.choice([1, 2, 5, 64, 65, 100, 127, 128]))

@@ -134,3 +134,9 @@ def test_trading_abi_validation_without_gpu():
     assert rc == _native.AM_ERR_INVALID and "round" in _native.last_error()
     rc = lib.am_check_player_moves(ctypes.byref(mk), 4100, 4096, None)
     assert rc == _native.AM_ERR_INVALID and "aligned" in _native.last_error()
+    # the allocation-free form checks the game's sizes before it touches a device
+    bad = _native.TradingDims(P, S, V, T + 1)
+    rc = lib.am_apply_player_trading_noalloc(ctypes.byref(mk), ctypes.byref(bad),
+                                             ctypes.byref(st), 4096, 0, 0, None, 4096, 4096,
+                                             4096, None)
+    assert rc == _native.AM_ERR_INVALID and _native.last_error()

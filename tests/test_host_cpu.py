@@ -1,8 +1,10 @@
 """Host-side checks that need no GPU: the C-ABI library loads and exports every
-symbol its header declares, argument validation raises like the reference,
+symbol its header declares, the headers are plain C that a C program links
+against, argument validation raises like the reference,
 the workload definitions and the bytes model hold together, and the fill
 record views map onto the right record words."""
 import ctypes
+import os
 
 import pytest
 import torch
@@ -16,6 +18,34 @@ def test_library_exports_every_header_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert lib.am_abi_version() == 2
+
+
+def test_headers_are_plain_c_and_link(tmp_path):
+    """include/*.h compile as strict C99 and every function they declare
+    links from a C program against the library: the boundary an FFI (cgo,
+    JNI, ctypes) binds needs no C++ and no torch."""
+    import subprocess
+    from astra_cuda import _build, _native
+    _native.lib()  # built and current
+    names = _native.header_functions()
+    src = ['#include "astra_market.h"', '#include "astra_trading.h"', "#include <stdio.h>",
+           "typedef void (*fn)(void);", "int main(void) {", "  const fn all[] = {"]
+    src += [f"    (fn){n}," for n in names]
+    src += ["  };", "  int n = 0;", "  for (unsigned i = 0; i < sizeof all / sizeof all[0]; ++i)",
+            "    n += all[i] != 0;", '  printf("%d %d\\n", n, am_abi_version());', "  return 0;",
+            "}"]
+    c = tmp_path / "abi.c"
+    c.write_text("\n".join(src) + "\n")
+    exe = str(tmp_path / "abi")
+    lib_dir = os.path.dirname(_build.LIB_PATH)
+    res = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                          "-I", _build.INCLUDE_DIR, str(c), "-o", exe, "-L",
+                          lib_dir, "-lastra_market", f"-Wl,-rpath,{lib_dir}"],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr[-3000:]
+    run = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    assert run.stdout.split() == [str(len(names)), "2"]
 
 
 def test_native_dims_validation_without_gpu():

@@ -517,3 +517,30 @@ def test_host_trading_body_reproduces_reference_game(lib):
                   f"{pre} end")
             _same("market_contract_over_time", mcot, z[f"{pre}/market_contract_over_time"],
                   f"{pre} end")
+
+
+def test_book_layout_regions(lib):
+    """The packed book's regions (am::layout_of, which am_book_bytes reports):
+    256-byte aligned, in order, each as large as its arrays, no overlap, for
+    sizes up to the limits (4 194 304 markets x 1024 slots is 137 GB of
+    records: 64-bit offsets)."""
+    from astra_cuda import _native
+    rng = np.random.default_rng(3)
+    dims = [(1, 1, 1), (4194304, 128, 1024), (1_000_000, 128, 512), (10_000, 128, 1024)]
+    dims += [(int(rng.integers(1, 4194305)), int(rng.integers(1, 129)), int(rng.integers(1, 1025)))
+             for _ in range(200)]
+    for N, L, O in dims:
+        lay = np.zeros(6, np.int64)
+        lib.hs_layout(N, L, O, lay.ctypes.data_as(_i64p))
+        slots, mask, levels, bbo, orders, total = (int(x) for x in lay)
+        need = [(slots, 4 * N), (mask, 32 * N), (levels, 8 * N * L), (bbo, 16 * N),
+                (orders, 32 * N * O)]
+        prev_end = 4  # the state-check flag word at offset 0
+        for off, size in need:
+            assert off % 256 == 0 and off >= prev_end, (N, L, O)
+            prev_end = off + size
+        assert total >= prev_end and total % 256 == 0 and total - prev_end < 256
+        nbytes = ctypes.c_uint64(0)
+        rc = _native.lib().am_book_bytes(ctypes.byref(_native.Dims(N, L, O, 1, 1)),
+                                         ctypes.byref(nbytes))
+        assert rc == 0 and nbytes.value == total, (N, L, O)
